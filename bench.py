@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of the fused TDA forward (BASELINE.json metric: "fused TDA fwd
+TFLOP/s & % bf16 tensor peak, S=8K D=128, at 1/2/4/8 B200").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tda|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (N > 1)
+
+Workload (default): threshold differential attention, bf16, q1,q2,k1,k2,v of
+shape (8, 32, 8192, 128) from seeded N(0,1), beta=1, lambda=0.5, p=2,
+normalize=True, causal.  The 256 (batch, head) slices are split over the N
+ranks (contiguous blocks, no collective on the data path); the total problem
+is fixed, so scaling is strong.
+
+One step = the key-norm pre-pass for k1 and k2 plus the fused forward kernel,
+on inputs resident in HBM (2.7 GB of inputs, larger than the 126 MB L2, so no
+flush is needed between steps).  FLOPs are the dense causal algorithmic count
+3*B*H*S^2*D (QK1, QK2 and one PV), never the executed count.
+
+Prints one JSON line on rank 0.  ``--impl reference`` times the CPU restatement
+of the reference (oracle/) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fused TDA fwd TFLOP/s & % bf16 tensor peak, S=8K D=128, at 1/2/4/8 B200"
+
+WORKLOADS = {
+    # name: (op, B, H, S, D, beta, lambda, p, normalize)
+    "diff8k": ("diff", 8, 32, 8192, 128, 1.0, 0.5, 2.0, True),
+    "rect8k": ("rect", 8, 32, 8192, 128, 1.0, 0.0, 2.0, True),
+    "rect4k": ("rect", 4, 32, 4096, 128, 1.0, 0.0, 2.0, True),
+    "diff32k": ("diff", 1, 16, 32768, 128, 1.5, 0.8, 2.0, True),
+}
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def flops_of(op, bh, S, D):
+    return (3.0 if op == "diff" else 2.0) * bh * float(S) ** 2 * D
+
+
+def describe(name):
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    lam_s = f" lambda={lam}" if op == "diff" else ""
+    return f"{op} bf16 ({B},{H},{S},{D}) beta={beta}{lam_s} p={p} normalize={norm} causal"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons during the
+    timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_smi_id(dev_index):
+    import torch
+    try:
+        u = torch.cuda.get_device_properties(dev_index).uuid
+        s = str(u)
+        return s if s.startswith("GPU-") else "GPU-" + s
+    except Exception:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            return vis.split(",")[dev_index]
+        return str(dev_index)
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_baseline(name, budget_s=10.0):
+    """The oracle's fp32 formula (the reference's algorithm restated on CPU)
+    on whole (batch, head) slices of the workload, one after another until the
+    time budget is spent.  Returns (TFLOP/s, cores, sample description)."""
+    import numpy as np
+    from oracle import tda_oracle as O
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        cores = os.cpu_count() or 1
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    rng = np.random.Generator(np.random.PCG64(1234))
+    n = 5 if op == "diff" else 3
+    done = 0
+    elapsed = 0.0  # compute time only (input generation excluded)
+    while elapsed < budget_s:
+        xs = [O.bf16_round(rng.standard_normal((1, 1, S, D), dtype=np.float32)) for _ in range(n)]
+        t = time.perf_counter()
+        if op == "diff":
+            O.diff_fwd(*xs, beta, lam, p, norm, dtype=np.float32)
+        else:
+            O.rect_fwd(*xs, beta, p, norm, dtype=np.float32)
+        elapsed += time.perf_counter() - t
+        done += 1
+    tf = flops_of(op, done, S, D) / elapsed / 1e12
+    sample = f"{done} of {B * H} (batch,head) slices, all {S} rows, numpy fp32 formula"
+    return tf, cores, sample, elapsed
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's algorithm on the host cores (the
+    CPU restatement in oracle/, since the reference itself is Triton-only)."""
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import tda_oracle as O
+    name = args.config
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:
+        cores = os.cpu_count() or 1
+    rng = np.random.Generator(np.random.PCG64(4321))
+    n = 5 if op == "diff" else 3
+    xs = [O.bf16_round(rng.standard_normal((1, 1, S, D), dtype=np.float32)) for _ in range(n)]
+    rows = np.arange(S - args.ref_rows, S)  # the last rows: each sees ~S keys
+
+    def step():
+        if op == "diff":
+            O.diff_fwd(*xs, beta, lam, p, norm, dtype=np.float32, rows=rows)
+        else:
+            O.rect_fwd(*xs, beta, p, norm, dtype=np.float32, rows=rows)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gemms = 3.0 if op == "diff" else 2.0
+    step_flops = gemms * 2.0 * D * float(np.sum(rows + 1))  # causal algorithmic work of the sampled rows
+    val = step_flops * args.steps / el / 1e12
+    sample = f"1 (batch,head) slice, last {args.ref_rows} of {S} query rows, numpy fp32 formula"
+    line = {
+        "metric": METRIC, "value": val, "unit": "TFLOP/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": describe(name), "sample": sample},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------- GPU arm
+def make_inputs(name, shard, device):
+    """Seeded N(0,1) inputs per (tensor, flattened head): identical data for a
+    given head whatever the number of ranks."""
+    import torch
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    n = 5 if op == "diff" else 3
+    xs = []
+    for t in range(n):
+        x = torch.empty((1, shard.size, S, D), dtype=torch.bfloat16, device=device)
+        for i, bh in enumerate(range(shard.start, shard.stop)):
+            g = torch.Generator(device=device).manual_seed(1_000_003 * (t + 1) + bh)
+            x[0, i] = torch.randn((S, D), generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+        xs.append(x)
+    return xs
+
+
+def run_tda(args, rank, local, world):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import tda_b200
+    from tda_b200 import _lib, ops
+    from tda_b200.shard import max_over_ranks, shard_range
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    name = args.config
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    shard = shard_range(B * H, world, rank)
+    xs = make_inputs(name, shard, dev)
+    n_bh = shard.size
+    lib = _lib.load()
+    status = ops._status_word(dev)
+    S_pad = (S + 127) // 128 * 128
+    out = torch.empty((1, n_bh, S, D), dtype=torch.bfloat16, device=dev)
+    rk = [torch.zeros(n_bh * S_pad, dtype=torch.float32, device=dev) for _ in range(2)]
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    ptr = [x.data_ptr() for x in xs]
+
+    def launch_norms():
+        if norm:
+            ks = (ptr[2], ptr[3]) if op == "diff" else (ptr[1],)
+            for kp, r in zip(ks, rk):
+                _lib.check(lib.tda_key_inv_norms(kp, _lib.TDA_BF16, n_bh, S, D, r.data_ptr(), sp))
+
+    def launch_main():
+        if op == "diff":
+            _lib.check(lib.tda_diff_fwd_tc(ptr[0], ptr[1], ptr[2], ptr[3], ptr[4], out.data_ptr(), _lib.TDA_BF16,
+                                           n_bh, S, D, beta, lam, p, int(norm), rk[0].data_ptr(),
+                                           rk[1].data_ptr(), status.data_ptr(), sp))
+        else:
+            _lib.check(lib.tda_rect_fwd_tc(ptr[0], ptr[1], ptr[2], out.data_ptr(), _lib.TDA_BF16, n_bh, S, D, beta,
+                                           p, int(norm), rk[0].data_ptr(), status.data_ptr(), sp))
+
+    launches_per_step = (2 if op == "diff" else 1) * int(norm) + 1
+
+    for _ in range(args.warmup):
+        launch_norms()
+        launch_main()
+    barrier()
+    ops.check_status(dev)
+
+    clocks = ClockSampler(gpu_smi_id(local)) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.4)  # let the sampler start before the timed region
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    barrier()
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        launch_norms()
+        ev[i][1].record(stream)
+        launch_main()
+        ev[i][2].record(stream)
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ops.check_status(dev)
+    total_ms = ev[0][0].elapsed_time(ev[-1][2])
+    main_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
+    norm_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
+    total_ms_max = max_over_ranks(total_ms, dev)
+    main_avg = statistics.mean(main_ms)
+    main_avg_max = max_over_ranks(main_avg, dev)
+
+    flops_total = flops_of(op, B * H, S, D)
+    value = flops_total * args.steps / (total_ms_max / 1e3) / 1e12
+    peaks, peak_src = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    achieved = flops_of(op, n_bh, S, D) / (main_avg / 1e3) / 1e12  # this rank's launch
+
+    # ---- end to end through the public API with pinned host buffers
+    host_in = [x.cpu().pin_memory() for x in xs]
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+    betat, lamt = torch.tensor(beta), torch.tensor(lam)
+
+    def e2e_step():
+        d = [h.to(dev, non_blocking=True) for h in host_in]
+        if op == "diff":
+            o = tda_b200.differential_threshold_rela_triton(*d, betat, lamt, p, norm)
+        else:
+            o = tda_b200.threshold_rela_triton(*d, betat, p, norm)
+        host_out.copy_(o, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    ops.check_status(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), dev)
+    e2e_val = flops_total * e2e_steps / (e2e_ms / 1e3) / 1e12
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, cores, sample, _ = cpu_baseline(name, args.cpu_budget)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+                traffic = json.load(f).get(name)
+        except Exception:
+            pass
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "impl": "tda",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": total_ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "pct_bf16_peak": value / world / peak,
+            "config": {
+                "workload": describe(name),
+                "batch": B, "heads": H, "seq_len": S, "head_dim": D,
+                "parallelism": f"(batch x head) shards over {world} GPU(s), no collective on the data path",
+                "flops_per_step": flops_total,
+                "l2": "inputs 2.7 GB > 126 MB L2; no flush",
+                "key_norm_ms_per_step": statistics.mean(norm_ms),
+                "main_kernel_ms": main_avg,
+                "main_kernel_ms_max_rank": main_avg_max,
+            },
+            "roofline": {
+                "bound": "tensor",
+                "achieved": achieved,
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "traffic": traffic,
+                "peak_source": f"bf16_tflops (burst) of {peak_src}",
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["tda", "reference"], default="tda")
+    ap.add_argument("--config", choices=sorted(WORKLOADS), default="diff8k")
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-rows", type=int, default=256, help="query rows per reference-arm step")
+    args = ap.parse_args()
+    from tda_b200.shard import env_rank_world
+    rank, local, world = env_rank_world()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_tda(args, rank, local, world)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,126 @@
+/*
+ * tda_b200 -- C ABI of the B200-native Threshold (Differential) Attention
+ * forward pass.
+ *
+ * These entry points are the drop-in boundary for the two public functions of
+ * the reference implementation (snap-research/TDA, triton_threshold_attention.py):
+ *
+ *   threshold_rela_triton(q, k, v, beta, relu_power)            :472-486
+ *   differential_threshold_rela_triton(q1, q2, k1, k2, v, beta,
+ *                                      lambda_param, relu_power,
+ *                                      normalize)                :489-519
+ *
+ * and of the launcher/kernel pair under them
+ * (ThresholdRelaFunction.forward :335-403, _threshold_rela_fwd_kernel :19-115).
+ *
+ * Conventions (all entry points):
+ *   - q, k, v, out are DEVICE pointers to contiguous (batch*heads, seq_len,
+ *     head_dim) row-major arrays, i.e. (B, H, S, D) tensors flattened over
+ *     (B, H).  All inputs share one shape (the reference asserts this, :348).
+ *   - dtype is TDA_F32 or TDA_BF16 for the inputs; out_dtype is the element
+ *     type written to out (equal to dtype, or TDA_F32 to receive the fp32
+ *     accumulator of a bf16 computation).
+ *   - Causal, with the reference's mask-to-zero semantics (:79-80):
+ *     out_i = sum_j relu(s_ij - tau_i)^p v_j, s_ij = q_i.k_j for j <= i and 0
+ *     for j > i, tau_i = beta * sqrt(2 * log(i + 1) / head_dim).
+ *   - stream is a cudaStream_t (NULL = legacy default stream).  Calls are
+ *     asynchronous and stream-ordered; no host synchronisation happens.
+ *   - status points to one device int32 that the kernels set to a nonzero
+ *     code when a bounded internal wait gives up (the output is then
+ *     invalid).  It is never cleared by the library.
+ *   - workspace is device scratch of at least tda_workspace_size() bytes
+ *     (may be NULL when that size is 0).  It is only used during the call.
+ *   - Return value: TDA_OK, or a negative TDA_ERR_* code with a message from
+ *     tda_last_error() (thread-local).
+ *
+ * Supported: dtype TDA_BF16 with head_dim 64 or 128 runs on the tcgen05
+ * tensor cores; dtype TDA_F32 with head_dim in {16, 32, 64, 128, 256} runs the
+ * exact-fp32 CUDA-core kernel.  Other combinations return
+ * TDA_ERR_UNSUPPORTED (the Python layer widens them to fp32 first).
+ */
+#ifndef TDA_B200_H_
+#define TDA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TDA_F32 0
+#define TDA_BF16 1
+
+#define TDA_OK 0
+#define TDA_ERR_INVALID (-1)     /* bad argument: shape, dtype, NULL or misaligned pointer */
+#define TDA_ERR_UNSUPPORTED (-2) /* valid but not implemented for this dtype / head_dim */
+#define TDA_ERR_CUDA (-3)        /* a CUDA runtime / driver call failed */
+#define TDA_ERR_WORKSPACE (-4)   /* workspace missing or too small */
+
+/* ABI version of this header (major * 100 + minor). */
+int tda_version(void);
+
+/* Thread-local description of the last error returned on this thread. */
+const char* tda_last_error(void);
+
+/* Device workspace bytes needed by tda_rect_fwd (differential = 0) or
+ * tda_diff_fwd (differential = 1) for these sizes.  Replaces the fp32 upcast
+ * copies the reference allocates per call (triton_threshold_attention.py:356-363):
+ * here only per-key inverse norms (normalize on the tensor-core path) are kept. */
+size_t tda_workspace_size(int differential, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim,
+                          int normalize);
+
+/* Threshold rectified attention forward.
+ * Replaces threshold_rela_triton (triton_threshold_attention.py:472-486) ->
+ * ThresholdRelaFunction.forward (:335-403) -> _threshold_rela_fwd_kernel (:19-115).
+ * normalize != 0 computes the reference applied to F.normalize(q), F.normalize(k)
+ * (as each branch of :505-512 does); the reference's own entry point has no
+ * such argument, normalize = 0 is its behaviour. */
+int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dtype, int out_dtype,
+                 int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,
+                 int normalize, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
+/* Threshold differential attention forward, fused into one pass over the keys:
+ * out = rect(q1, k1, v) - clamp(lambda, 0, 1) * rect(q2, k2, v).
+ * Replaces differential_threshold_rela_triton (triton_threshold_attention.py:489-519),
+ * which runs F.normalize x4 (:505-509), the forward kernel twice (:512-513) and
+ * the clamp/combine (:516-517). */
+int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
+                 int dtype, int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta,
+                 float lambda_param, float relu_power, int normalize, void* workspace, size_t workspace_bytes,
+                 int* status, void* stream);
+
+/* Stage 1 of the normalized tensor-core path, exposed so callers can time or
+ * reuse it: rk[bh * pad + j] = 1 / max(||k[bh][j]||, 1e-12) for j < seq_len and
+ * 0 up to pad = seq_len rounded up to 128.  rk holds batch_heads * pad floats.
+ * This is the key half of F.normalize (triton_threshold_attention.py:507,509). */
+int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float* rk,
+                      void* stream);
+
+/* Stage 2 of tda_rect_fwd on the tensor-core path (dtype TDA_BF16), given the
+ * key inverse norms from tda_key_inv_norms (ignored, may be NULL, when
+ * normalize = 0).  Same semantics as tda_rect_fwd
+ * (triton_threshold_attention.py:19-115, :335-403). */
+int tda_rect_fwd_tc(const void* q, const void* k, const void* v, void* out, int out_dtype, int64_t batch_heads,
+                    int64_t seq_len, int64_t head_dim, float beta, float relu_power, int normalize,
+                    const float* rk, int* status, void* stream);
+
+/* Stage 2 of tda_diff_fwd on the tensor-core path (dtype TDA_BF16), given the
+ * inverse norms of k1 (rk1) and k2 (rk2).  Same semantics as tda_diff_fwd
+ * (triton_threshold_attention.py:489-519). */
+int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
+                    int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta,
+                    float lambda_param, float relu_power, int normalize, const float* rk1, const float* rk2,
+                    int* status, void* stream);
+
+/* Test hook (no counterpart in the reference): inject = 1 makes the next
+ * tensor-core launches skip their Q load so every internal wait times out
+ * after wait_timeout_ns; inject = 0 restores normal operation.  A
+ * wait_timeout_ns of 0 keeps the default (1 s).  Process-wide setting. */
+int tda_debug_set(int inject, uint64_t wait_timeout_ns);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TDA_B200_H_ */

@@ -1,0 +1,259 @@
+// extern "C" entry points declared in include/tda_b200.h: argument checks,
+// TMA descriptor construction and stream-ordered launches.  No allocation, no
+// host synchronisation.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/tda_b200.h"
+#include "tda_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<int> g_inject{0};
+std::atomic<unsigned long long> g_timeout_ns{1000000000ull};
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(TDA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// (BH, S, D) bf16 array viewed as 3-D {D, S, BH}; box {64, 128, 1}; 128-B swizzle.
+int make_map(CUtensorMap* m, const void* base, int64_t BH, int64_t S, int64_t D) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(S * D * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(tda::kTile), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return TDA_OK;
+}
+
+int check_common(int64_t BH, int64_t S, int64_t D, int* status) {
+  if (BH < 1 || S < 1) return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1 (got %lld, %lld)",
+                                   static_cast<long long>(BH), static_cast<long long>(S));
+  if (D < 16 || D > 256 || (D & (D - 1)) != 0)
+    return fail(TDA_ERR_INVALID, "head_dim must be a power of two in [16, 256] (got %lld)", static_cast<long long>(D));
+  if (S > (1ll << 30)) return fail(TDA_ERR_INVALID, "seq_len too large (%lld)", static_cast<long long>(S));
+  const int64_t tiles = BH * ((S + 63) / 64);
+  if (tiles > 0x7fffffffll) return fail(TDA_ERR_INVALID, "batch_heads * seq_len tiles exceed the grid limit");
+  if (!status) return fail(TDA_ERR_INVALID, "status must point to a device int32");
+  return TDA_OK;
+}
+
+bool tc_supported(int dtype, int64_t D) { return dtype == TDA_BF16 && (D == 64 || D == 128); }
+
+int run_tc(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int out_dtype,
+           int64_t BH, int64_t S, int64_t D, float beta, float lam, float p, int normalize, const float* rk1,
+           const float* rk2, int* status, void* stream, bool differential) {
+  if (int e = check_common(BH, S, D, status)) return e;
+  if (!(D == 64 || D == 128)) return fail(TDA_ERR_UNSUPPORTED, "tensor-core path needs head_dim 64 or 128");
+  if (out_dtype != TDA_BF16 && out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "out_dtype must be TDA_BF16 or TDA_F32");
+  const void* ins[5] = {q1, k1, v, differential ? q2 : q1, differential ? k2 : k1};
+  for (const void* x : ins)
+    if (!x || !aligned16(x)) return fail(TDA_ERR_INVALID, "inputs must be non-NULL and 16-byte aligned");
+  if (!out || !aligned16(out)) return fail(TDA_ERR_INVALID, "out must be non-NULL and 16-byte aligned");
+  if (normalize && (!rk1 || (differential && !rk2) || !aligned16(rk1) || (differential && !aligned16(rk2))))
+    return fail(TDA_ERR_INVALID, "normalize needs 16-byte aligned key inverse norms");
+  if (!(p == p)) return fail(TDA_ERR_INVALID, "relu_power is NaN");
+
+  tda::TcFwdParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+  int e;
+  if ((e = make_map(&prm.tm_q1, q1, BH, S, D))) return e;
+  if ((e = make_map(&prm.tm_k1, k1, BH, S, D))) return e;
+  if ((e = make_map(&prm.tm_v, v, BH, S, D))) return e;
+  if (differential) {
+    if ((e = make_map(&prm.tm_q2, q2, BH, S, D))) return e;
+    if ((e = make_map(&prm.tm_k2, k2, BH, S, D))) return e;
+  }
+  prm.rk1 = rk1;
+  prm.rk2 = rk2;
+  prm.out = out;
+  prm.status = status;
+  prm.S = static_cast<int>(S);
+  prm.S_pad = static_cast<int>(tda::padded_seq(S));
+  prm.BH = static_cast<int>(BH);
+  prm.n_qtiles = static_cast<int>((S + tda::kTile - 1) / tda::kTile);
+  prm.out_f32 = out_dtype == TDA_F32;
+  prm.causal_skip = beta >= 0.0f ? 1 : 0;
+  prm.beta = beta;
+  prm.relu_power = p;
+  prm.lam = lam;
+  prm.tau_scale = 2.0f / static_cast<float>(D);
+  prm.timeout_ns = g_timeout_ns.load();
+  prm.inject = g_inject.load();
+  cudaError_t ce = tda::launch_tc_fwd(prm, static_cast<int>(D), differential, normalize != 0, tda::pow_mode_of(p),
+                                      static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core forward launch");
+  return TDA_OK;
+}
+
+int run_simt(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int64_t BH,
+             int64_t S, int64_t D, float beta, float lam, float p, int normalize, int* status, void* stream,
+             bool differential) {
+  if (int e = check_common(BH, S, D, status)) return e;
+  const void* ins[5] = {q1, k1, v, differential ? q2 : q1, differential ? k2 : k1};
+  for (const void* x : ins)
+    if (!x || !aligned16(x)) return fail(TDA_ERR_INVALID, "inputs must be non-NULL and 16-byte aligned");
+  if (!out || !aligned16(out)) return fail(TDA_ERR_INVALID, "out must be non-NULL and 16-byte aligned");
+  tda::SimtFwdParams prm;
+  prm.q1 = static_cast<const float*>(q1);
+  prm.k1 = static_cast<const float*>(k1);
+  prm.q2 = static_cast<const float*>(differential ? q2 : q1);
+  prm.k2 = static_cast<const float*>(differential ? k2 : k1);
+  prm.v = static_cast<const float*>(v);
+  prm.out = static_cast<float*>(out);
+  prm.S = static_cast<int>(S);
+  prm.BH = static_cast<int>(BH);
+  prm.beta = beta;
+  prm.relu_power = p;
+  prm.lam = lam;
+  prm.normalize = normalize != 0;
+  prm.differential = differential;
+  cudaError_t ce = tda::launch_simt_fwd(prm, static_cast<int>(D), static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "fp32 forward launch");
+  return TDA_OK;
+}
+
+float clamp01(float x) { return x < 0.0f ? 0.0f : (x > 1.0f ? 1.0f : x); }
+
+size_t rk_bytes(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * tda::padded_seq(S) * sizeof(float); }
+
+}  // namespace
+
+extern "C" {
+
+int tda_version(void) { return 100; }
+
+const char* tda_last_error(void) { return g_last_error.c_str(); }
+
+int tda_debug_set(int inject, uint64_t wait_timeout_ns) {
+  g_inject.store(inject);
+  g_timeout_ns.store(wait_timeout_ns ? wait_timeout_ns : 1000000000ull);
+  return TDA_OK;
+}
+
+size_t tda_workspace_size(int differential, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim,
+                          int normalize) {
+  if (!normalize || !tc_supported(dtype, head_dim) || batch_heads < 1 || seq_len < 1) return 0;
+  const size_t one = (rk_bytes(batch_heads, seq_len) + 255) / 256 * 256;
+  return differential ? 2 * one : one;
+}
+
+int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float* rk,
+                      void* stream) {
+  if (batch_heads < 1 || seq_len < 1) return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1");
+  if (!tc_supported(dtype, head_dim)) return fail(TDA_ERR_UNSUPPORTED, "key norms need bf16 with head_dim 64 or 128");
+  if (!k || !rk || !aligned16(k) || !aligned16(rk)) return fail(TDA_ERR_INVALID, "k / rk must be 16-byte aligned");
+  cudaError_t ce = tda::launch_key_norms(k, 1, rk, static_cast<int>(batch_heads), static_cast<int>(seq_len),
+                                         static_cast<int>(tda::padded_seq(seq_len)), static_cast<int>(head_dim),
+                                         static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "key norm launch");
+  return TDA_OK;
+}
+
+int tda_rect_fwd_tc(const void* q, const void* k, const void* v, void* out, int out_dtype, int64_t batch_heads,
+                    int64_t seq_len, int64_t head_dim, float beta, float relu_power, int normalize,
+                    const float* rk, int* status, void* stream) {
+  return run_tc(q, nullptr, k, nullptr, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, 0.0f, relu_power,
+                normalize, rk, nullptr, status, stream, false);
+}
+
+int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
+                    int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta,
+                    float lambda_param, float relu_power, int normalize, const float* rk1, const float* rk2,
+                    int* status, void* stream) {
+  return run_tc(q1, q2, k1, k2, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, clamp01(lambda_param),
+                relu_power, normalize, rk1, rk2, status, stream, true);
+}
+
+int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dtype, int out_dtype,
+                 int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,
+                 int normalize, void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  if (dtype == TDA_F32) {
+    if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
+    return run_simt(q, nullptr, k, nullptr, v, out, batch_heads, seq_len, head_dim, beta, 0.0f, relu_power,
+                    normalize, status, stream, false);
+  }
+  if (dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
+  if (!tc_supported(dtype, head_dim))
+    return fail(TDA_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
+                static_cast<long long>(head_dim));
+  float* rk = nullptr;
+  if (normalize) {
+    const size_t need = tda_workspace_size(0, dtype, batch_heads, seq_len, head_dim, normalize);
+    if (!workspace || workspace_bytes < need)
+      return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+    rk = static_cast<float*>(workspace);
+    if (int e = tda_key_inv_norms(k, dtype, batch_heads, seq_len, head_dim, rk, stream)) return e;
+  }
+  return tda_rect_fwd_tc(q, k, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, relu_power, normalize, rk,
+                         status, stream);
+}
+
+int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
+                 int dtype, int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta,
+                 float lambda_param, float relu_power, int normalize, void* workspace, size_t workspace_bytes,
+                 int* status, void* stream) {
+  if (dtype == TDA_F32) {
+    if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
+    return run_simt(q1, q2, k1, k2, v, out, batch_heads, seq_len, head_dim, beta, clamp01(lambda_param),
+                    relu_power, normalize, status, stream, true);
+  }
+  if (dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
+  if (!tc_supported(dtype, head_dim))
+    return fail(TDA_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
+                static_cast<long long>(head_dim));
+  float* rk1 = nullptr;
+  float* rk2 = nullptr;
+  if (normalize) {
+    const size_t need = tda_workspace_size(1, dtype, batch_heads, seq_len, head_dim, normalize);
+    if (!workspace || workspace_bytes < need)
+      return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+    rk1 = static_cast<float*>(workspace);
+    rk2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2);
+    if (int e = tda_key_inv_norms(k1, dtype, batch_heads, seq_len, head_dim, rk1, stream)) return e;
+    if (int e = tda_key_inv_norms(k2, dtype, batch_heads, seq_len, head_dim, rk2, stream)) return e;
+  }
+  return tda_diff_fwd_tc(q1, q2, k1, k2, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, lambda_param,
+                         relu_power, normalize, rk1, rk2, status, stream);
+}
+
+}  // extern "C"

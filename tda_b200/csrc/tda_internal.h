@@ -1,0 +1,80 @@
+// Internal (non-exported) launch interfaces shared by the kernel translation
+// units and the C-ABI layer.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace tda {
+
+// Power-of-ReLU specialisations (triton_threshold_attention.py:89-101).
+enum PowMode : int { POW_1 = 0, POW_2 = 1, POW_3 = 2, POW_GENERAL = 3 };
+
+inline int pow_mode_of(float p) {
+  if (p == 1.0f) return POW_1;
+  if (p == 2.0f) return POW_2;
+  if (p == 3.0f) return POW_3;
+  return POW_GENERAL;
+}
+
+// Query/key tile edge of the tensor-core kernels (one UMMA M / one key block).
+constexpr int kTile = 128;
+
+inline int64_t padded_seq(int64_t S) { return (S + kTile - 1) / kTile * kTile; }
+
+// Tensor-core (tcgen05) forward, bf16 storage.  q/k/v tensor maps view the
+// (batch*heads, S, D) arrays as 3-D {D, S, BH} with a {64, 128, 1} box and
+// 128-byte swizzle.
+struct TcFwdParams {
+  CUtensorMap tm_q1;
+  CUtensorMap tm_q2;  // differential only
+  CUtensorMap tm_k1;
+  CUtensorMap tm_k2;  // differential only
+  CUtensorMap tm_v;
+  const float* rk1;   // [BH][S_pad] 1/max(||k1_j||, eps), 0 in the padding (normalize only)
+  const float* rk2;   // same for k2 (differential + normalize)
+  void* out;          // [BH][S][D], bf16 or f32 (out_f32)
+  int* status;        // device status word; nonzero after a bounded wait gave up
+  int S;
+  int S_pad;
+  int BH;
+  int n_qtiles;
+  int out_f32;
+  int causal_skip;    // 1 when beta >= 0: key tiles past the diagonal contribute 0
+  float beta;
+  float relu_power;
+  float lam;          // clamped lambda (differential)
+  float tau_scale;    // 2 / D
+  unsigned long long timeout_ns;
+  int inject;         // test hook: bit 0 = producer never loads Q (forces a timeout)
+};
+
+cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,
+                          cudaStream_t stream);
+
+// CUDA-core fp32 forward (exact fp32 FFMA), any power-of-two D in [16, 256].
+struct SimtFwdParams {
+  const float* q1;
+  const float* k1;
+  const float* q2;  // differential only
+  const float* k2;  // differential only
+  const float* v;
+  float* out;
+  int S;
+  int BH;
+  float beta;
+  float relu_power;
+  float lam;
+  int normalize;
+  int differential;
+};
+
+cudaError_t launch_simt_fwd(const SimtFwdParams& p, int head_dim, cudaStream_t stream);
+
+// rk[bh][j] = 1 / max(||x[bh][j]||_2, 1e-12) for j < S, 0 for S <= j < S_pad.
+cudaError_t launch_key_norms(const void* x, int x_is_bf16, float* rk, int BH, int S, int S_pad, int D,
+                             cudaStream_t stream);
+
+}  // namespace tda

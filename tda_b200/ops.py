@@ -1,0 +1,208 @@
+"""Host-side mirror of the reference TDA interface (snap-research/TDA,
+``triton_threshold_attention.py``), backed by the tda_b200 C ABI.
+
+Public functions keep the reference's names, argument meaning and error
+behaviour:
+
+* ``threshold_rela_triton(q, k, v, beta, relu_power=2.0, normalize=False)``
+  -- reference :472-486.  ``normalize`` is an added trailing keyword; its
+  default (False) is the reference's behaviour, True equals the reference
+  called on F.normalize(q), F.normalize(k).
+* ``differential_threshold_rela_triton(q1, q2, k1, k2, v, beta, lambda_param,
+  relu_power=2.0, normalize=True)`` -- reference :489-519, computed in ONE
+  fused pass over the keys (one launch instead of two forward kernels plus
+  the torch normalize / clamp / combine ops).
+* ``ThresholdRelaFunction`` -- reference :327-469 (forward only here; its
+  backward raises NotImplementedError).
+
+Data path: CUDA tensors only.  bf16 with head_dim 64/128 runs the tcgen05
+tensor-core kernel; fp32 runs the exact-fp32 CUDA-core kernel; other dtypes /
+head dims are widened to fp32 on the device.  There is no CPU fallback: CPU
+tensors raise, and a missing CUDA library raises.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+
+_STATUS: dict[int, torch.Tensor] = {}
+_SYNC_CHECK = os.environ.get("TDA_B200_SYNC_CHECK", "0") not in ("", "0")
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _STATUS[idx] = t
+    return t
+
+
+def check_status(device=None, reset: bool = True) -> None:
+    """Synchronise ``device`` and raise if any tda_b200 kernel on it reported a
+    bounded wait that gave up (its output is then invalid).  Clears the word
+    when ``reset``."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    word = _status_word(dev)
+    code = int(word.item())
+    if code != 0:
+        if reset:
+            word.zero_()
+        raise _lib.TdaError(f"tda_b200 kernel aborted after a wait timeout (status 0x{code:x})")
+
+
+def _scalar(x) -> float:
+    # reference :352-353: Tensor -> .item(), else float()
+    return float(x.item()) if isinstance(x, torch.Tensor) else float(x)
+
+
+def _plan(tensors, what: str):
+    """Validate device / shape and pick the kernel path.  Returns
+    (kind, compute_tensors, orig_dtype)."""
+    t0 = tensors[0]
+    for t in tensors:
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{what}: expected torch.Tensor inputs")
+    if t0.dim() != 4:
+        raise ValueError(f"{what}: expected (batch, num_heads, seq_len, head_dim) tensors, got {tuple(t0.shape)}")
+    if not t0.is_cuda:
+        raise RuntimeError(f"{what}: tda_b200 runs on CUDA tensors only (got device {t0.device}); "
+                           "there is no CPU fallback")
+    for t in tensors:
+        if t.device != t0.device:
+            raise RuntimeError(f"{what}: all inputs must be on one device")
+    orig = t0.dtype
+    common = tensors[0].dtype
+    for t in tensors[1:]:
+        common = torch.promote_types(common, t.dtype)
+    if not common.is_floating_point:
+        raise TypeError(f"{what}: floating point inputs required, got {common}")
+    D = t0.shape[-1]
+    if D < 16 or D > 256 or (D & (D - 1)) != 0:
+        raise ValueError(f"{what}: head_dim must be a power of two in [16, 256], got {D}")
+    if common == torch.bfloat16 and D in (64, 128):
+        kind, cdt = _lib.TDA_BF16, torch.bfloat16
+    else:
+        kind, cdt = _lib.TDA_F32, torch.float32
+    comp = [t.to(cdt).contiguous() for t in tensors]
+    return kind, comp, orig
+
+
+def _finish(out: torch.Tensor, orig: torch.dtype, out_dtype) -> torch.Tensor:
+    want = orig if out_dtype is None else out_dtype
+    if out.dtype != want:
+        out = out.to(want)
+    if _SYNC_CHECK:
+        check_status(out.device)
+    return out
+
+
+def rect_forward(q, k, v, beta, relu_power=2.0, normalize: bool = False, out_dtype=None) -> torch.Tensor:
+    """Threshold rectified attention forward (no autograd).  ``out_dtype``
+    (default: q's dtype) may be torch.float32 on the bf16 path to receive the
+    kernel's fp32 accumulator."""
+    # reference :348
+    assert q.shape == k.shape == v.shape
+    beta_v = _scalar(beta)
+    p_v = _scalar(relu_power)
+    kind, (qc, kc, vc), orig = _plan([q, k, v], "threshold_rela_triton")
+    B, H, S, D = qc.shape
+    raw_dt = torch.float32 if (kind == _lib.TDA_F32 or out_dtype == torch.float32) else torch.bfloat16
+    out = torch.empty((B, H, S, D), dtype=raw_dt, device=qc.device)
+    if out.numel() == 0:
+        return _finish(out, orig, out_dtype)
+    lib = _lib.load()
+    ws_n = lib.tda_workspace_size(0, kind, B * H, S, D, int(normalize))
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=qc.device) if ws_n else None
+    stream = torch.cuda.current_stream(qc.device).cuda_stream
+    out_kind = _lib.TDA_F32 if raw_dt == torch.float32 else _lib.TDA_BF16
+    with torch.cuda.device(qc.device):
+        rc = lib.tda_rect_fwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), kind, out_kind,
+                              B * H, S, D, beta_v, p_v, int(normalize),
+                              ws.data_ptr() if ws is not None else None, ws_n,
+                              _status_word(qc.device).data_ptr(), stream)
+    _lib.check(rc)
+    return _finish(out, orig, out_dtype)
+
+
+def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normalize: bool = True,
+                 out_dtype=None) -> torch.Tensor:
+    """Threshold differential attention forward (no autograd), fused."""
+    assert q1.shape == q2.shape == k1.shape == k2.shape == v.shape
+    beta_v = _scalar(beta)
+    p_v = _scalar(relu_power)
+    if isinstance(lambda_param, torch.Tensor) and lambda_param.numel() != 1:
+        # A broadcastable (e.g. per-head) lambda: the reference's combine
+        # out1 - clamp(lambda) * out2 (:516-517) applied to two fused passes.
+        o1 = rect_forward(q1, k1, v, beta_v, p_v, normalize, out_dtype=torch.float32)
+        o2 = rect_forward(q2, k2, v, beta_v, p_v, normalize, out_dtype=torch.float32)
+        lam = torch.clamp(lambda_param.to(device=o1.device, dtype=torch.float32), min=0.0, max=1.0)
+        return _finish(o1 - lam * o2, q1.dtype, out_dtype)
+    lam_v = _scalar(lambda_param)
+    kind, (a, b, c, d, e), orig = _plan([q1, q2, k1, k2, v], "differential_threshold_rela_triton")
+    B, H, S, D = a.shape
+    raw_dt = torch.float32 if (kind == _lib.TDA_F32 or out_dtype == torch.float32) else torch.bfloat16
+    out = torch.empty((B, H, S, D), dtype=raw_dt, device=a.device)
+    if out.numel() == 0:
+        return _finish(out, orig, out_dtype)
+    lib = _lib.load()
+    ws_n = lib.tda_workspace_size(1, kind, B * H, S, D, int(normalize))
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=a.device) if ws_n else None
+    stream = torch.cuda.current_stream(a.device).cuda_stream
+    out_kind = _lib.TDA_F32 if raw_dt == torch.float32 else _lib.TDA_BF16
+    with torch.cuda.device(a.device):
+        rc = lib.tda_diff_fwd(a.data_ptr(), b.data_ptr(), c.data_ptr(), d.data_ptr(), e.data_ptr(), out.data_ptr(),
+                              kind, out_kind, B * H, S, D, beta_v, lam_v, p_v, int(normalize),
+                              ws.data_ptr() if ws is not None else None, ws_n,
+                              _status_word(a.device).data_ptr(), stream)
+    _lib.check(rc)
+    return _finish(out, orig, out_dtype)
+
+
+class ThresholdRelaFunction(torch.autograd.Function):
+    """Threshold Rectified Attention (reference :327-469).
+
+    forward(q, k, v, beta, relu_power[, normalize]) -> out.  The backward pass
+    is not implemented yet and raises NotImplementedError instead of
+    returning wrong or missing gradients."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, beta, relu_power, normalize=False):
+        return rect_forward(q, k, v, beta, relu_power, normalize)
+
+    @staticmethod
+    def backward(ctx, dout):
+        raise NotImplementedError("tda_b200: the backward pass of threshold attention is not implemented")
+
+
+class DifferentialThresholdRelaFunction(torch.autograd.Function):
+    """Fused threshold differential attention; forward only (backward raises)."""
+
+    @staticmethod
+    def forward(ctx, q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize):
+        return diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize)
+
+    @staticmethod
+    def backward(ctx, dout):
+        raise NotImplementedError("tda_b200: the backward pass of threshold attention is not implemented")
+
+
+def threshold_rela_triton(q, k, v, beta, relu_power=2.0, normalize=False):
+    """Threshold Rectified Attention: out = ReLU(Q K^T - tau)^p V, causal.
+
+    q, k, v: (batch, num_heads, seq_len, head_dim); beta: scalar tensor or
+    float; relu_power: scalar (default 2.0); normalize: L2-normalize q and k
+    first (default False, the reference's behaviour).  Returns a tensor of
+    q's shape and dtype."""
+    return ThresholdRelaFunction.apply(q, k, v, beta, relu_power, normalize)
+
+
+def differential_threshold_rela_triton(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normalize=True):
+    """Threshold Differential Attention:
+    out = TRA(q1, k1, v) - clamp(lambda, 0, 1) * TRA(q2, k2, v), with q/k
+    L2-normalized when ``normalize`` (default True).  Returns q1's shape and
+    dtype."""
+    return DifferentialThresholdRelaFunction.apply(q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize)
