@@ -113,6 +113,23 @@ int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* 
                     float lambda_param, float relu_power, int normalize, const float* rk1, const float* rk2,
                     int* status, void* stream);
 
+/* Same computation and arguments as tda_diff_fwd, minus the workspace: for
+ * callers that cannot allocate device memory -- e.g. code running inside an
+ * allocator or memory-pool callback (allocating there would re-enter the
+ * allocator), runtimes that forbid allocation after start-up, or plugins whose
+ * host owns all device memory and passes only inputs and outputs.  No
+ * counterpart in the reference (which allocates fp32 copies on every call).
+ * The scratch (inverse key norms) lives in a fixed 8 MiB array inside the
+ * library, reserved on every GPU that loads it: requires
+ * batch_heads * round_up(seq_len, 128) <= 1048576, else TDA_ERR_INVALID.
+ * Makes no cudaMalloc / cudaFree call.  The first call on a device looks up
+ * the array's address (do it before any stream capture).  All calls share the
+ * array: calls whose GPU work overlaps race and must be ordered on one stream. */
+int tda_diff_fwd_noalloc(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
+                         int dtype, int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim,
+                         float beta, float lambda_param, float relu_power, int normalize, int* status,
+                         void* stream);
+
 /* Test hook (no counterpart in the reference): inject = 1 makes the next
  * tensor-core launches skip their Q load so every internal wait times out
  * after wait_timeout_ns; inject = 0 restores normal operation.  A

@@ -158,6 +158,8 @@ size_t rk_bytes(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * tda::p
 
 }  // namespace
 
+void tda::set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
+
 extern "C" {
 
 int tda_version(void) { return 100; }

@@ -77,4 +77,7 @@ cudaError_t launch_simt_fwd(const SimtFwdParams& p, int head_dim, cudaStream_t s
 cudaError_t launch_key_norms(const void* x, int x_is_bf16, float* rk, int BH, int S, int S_pad, int D,
                              cudaStream_t stream);
 
+// Sets the thread-local message returned by tda_last_error().
+void set_last_error(const char* msg);
+
 }  // namespace tda
