@@ -6,6 +6,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -116,11 +117,15 @@ int run_tc(const void* q1, const void* q2, const void* k1, const void* k2, const
   prm.beta = beta;
   prm.relu_power = p;
   prm.lam = lam;
+  prm.lam_root = p == 2.0f ? std::sqrt(lam) : (p == 3.0f ? std::cbrt(lam) : lam);
   prm.tau_scale = 2.0f / static_cast<float>(D);
   prm.timeout_ns = g_timeout_ns.load();
   prm.inject = g_inject.load();
   cudaError_t ce = tda::launch_tc_fwd(prm, static_cast<int>(D), differential, normalize != 0, tda::pow_mode_of(p),
                                       static_cast<cudaStream_t>(stream));
+  if (ce == cudaErrorLaunchOutOfResources && !g_last_error.empty() &&
+      g_last_error.rfind("tensor-core kernel does not fit", 0) == 0)
+    return TDA_ERR_CUDA;
   if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core forward launch");
   return TDA_OK;
 }

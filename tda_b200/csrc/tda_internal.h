@@ -46,6 +46,7 @@ struct TcFwdParams {
   float beta;
   float relu_power;
   float lam;          // clamped lambda (differential)
+  float lam_root;     // lambda^(1/p) for p in {1, 2, 3} (folded into the second branch)
   float tau_scale;    // 2 / D
   unsigned long long timeout_ns;
   int inject;         // test hook: bit 0 = producer never loads Q (forces a timeout)
