@@ -132,17 +132,25 @@ def gpu_smi_id(dev_index):
 
 
 # ------------------------------------------------------------- CPU baseline
+def _use_all_cores():
+    """Give numpy's BLAS every host core (torchrun sets OMP_NUM_THREADS=1).
+    Returns the thread count in effect."""
+    n = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        threadpool_limits(limits=n)
+        return max((i.get("num_threads", 1) for i in threadpool_info()), default=n)
+    except Exception:
+        return n
+
+
 def cpu_baseline(name, budget_s=10.0):
     """The oracle's fp32 formula (the reference's algorithm restated on CPU)
     on whole (batch, head) slices of the workload, one after another until the
     time budget is spent.  Returns (TFLOP/s, cores, sample description)."""
     import numpy as np
     from oracle import tda_oracle as O
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-    except Exception:
-        cores = os.cpu_count() or 1
+    cores = _use_all_cores()
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
     rng = np.random.Generator(np.random.PCG64(1234))
     n = 5 if op == "diff" else 3
@@ -171,11 +179,7 @@ def run_reference(args, rank, world):
     from oracle import tda_oracle as O
     name = args.config
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-    except Exception:
-        cores = os.cpu_count() or 1
+    cores = _use_all_cores()
     rng = np.random.Generator(np.random.PCG64(4321))
     n = 5 if op == "diff" else 3
     xs = [O.bf16_round(rng.standard_normal((1, 1, S, D), dtype=np.float32)) for _ in range(n)]
