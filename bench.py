@@ -258,7 +258,7 @@ def run_tda(args, rank, local, world):
     status = ops._status_word(dev)
     S_pad = (S + 127) // 128 * 128
     out = torch.empty((1, n_bh, S, D), dtype=torch.bfloat16, device=dev)
-    rk = [torch.zeros(n_bh * S_pad, dtype=torch.float32, device=dev) for _ in range(2)]
+    rk = [torch.zeros(n_bh * S_pad // 16 * 17, dtype=torch.float32, device=dev) for _ in range(2)]  # key tables
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     ptr = [x.data_ptr() for x in xs]

@@ -91,8 +91,11 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                  int* status, void* stream);
 
 /* Stage 1 of the normalized tensor-core path, exposed so callers can time or
- * reuse it: rk[bh * pad + j] = 1 / max(||k[bh][j]||, 1e-12) for j < seq_len and
- * 0 up to pad = seq_len rounded up to 128.  rk holds batch_heads * pad floats.
+ * reuse it.  Writes the key table of k into rk (batch_heads * pad * 17 / 16
+ * floats, pad = seq_len rounded up to 128): rk[bh * pad + j] =
+ * 1 / max(||k[bh][j]||, 1e-12) for j < seq_len and 0 up to pad, followed by
+ * rk[batch_heads * pad + bh * pad / 16 + g] = the maximum of those inverse norms
+ * over keys [16 g, 16 g + 16).
  * This is the key half of F.normalize (triton_threshold_attention.py:507,509). */
 int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float* rk,
                       void* stream);
@@ -119,7 +122,7 @@ int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* 
  * allocator), runtimes that forbid allocation after start-up, or plugins whose
  * host owns all device memory and passes only inputs and outputs.  No
  * counterpart in the reference (which allocates fp32 copies on every call).
- * The scratch (inverse key norms) lives in a fixed 8 MiB array inside the
+ * The scratch (inverse key norms) lives in a fixed 8.5 MiB array inside the
  * library, reserved on every GPU that loads it: requires
  * batch_heads * round_up(seq_len, 128) <= 1048576, else TDA_ERR_INVALID.
  * Makes no cudaMalloc / cudaFree call.  The first call on a device looks up

@@ -159,7 +159,7 @@ int run_simt(const void* q1, const void* q2, const void* k1, const void* k2, con
 
 float clamp01(float x) { return x < 0.0f ? 0.0f : (x > 1.0f ? 1.0f : x); }
 
-size_t rk_bytes(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * tda::padded_seq(S) * sizeof(float); }
+size_t rk_bytes(int64_t BH, int64_t S) { return tda::key_table_floats(BH, S) * sizeof(float); }
 
 }  // namespace
 

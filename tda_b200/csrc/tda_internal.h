@@ -33,7 +33,7 @@ struct TcFwdParams {
   CUtensorMap tm_k1;
   CUtensorMap tm_k2;  // differential only
   CUtensorMap tm_v;
-  const float* rk1;   // [BH][S_pad] 1/max(||k1_j||, eps), 0 in the padding (normalize only)
+  const float* rk1;   // key table of k1 (normalize only): rk [BH][S_pad] then rkmax [BH][S_pad/16]
   const float* rk2;   // same for k2 (differential + normalize)
   void* out;          // [BH][S][D], bf16 or f32 (out_f32)
   int* status;        // device status word; nonzero after a bounded wait gave up
@@ -55,6 +55,7 @@ struct TcFwdParams {
 cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,
                           cudaStream_t stream);
 
+
 // CUDA-core fp32 forward (exact fp32 FFMA), any power-of-two D in [16, 256].
 struct SimtFwdParams {
   const float* q1;
@@ -74,7 +75,9 @@ struct SimtFwdParams {
 
 cudaError_t launch_simt_fwd(const SimtFwdParams& p, int head_dim, cudaStream_t stream);
 
-// rk[bh][j] = 1 / max(||x[bh][j]||_2, 1e-12) for j < S, 0 for S <= j < S_pad.
+// Key table of x: rk[bh][j] = 1 / max(||x[bh][j]||_2, 1e-12) for j < S, 0 for
+// S <= j < S_pad, followed by rkmax[bh][g] = max of rk over keys [16 g, 16 g + 16).
+inline size_t key_table_floats(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * padded_seq(S) / 16 * 17; }
 cudaError_t launch_key_norms(const void* x, int x_is_bf16, float* rk, int BH, int S, int S_pad, int D,
                              cudaStream_t stream);
 

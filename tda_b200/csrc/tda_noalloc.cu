@@ -12,7 +12,7 @@
 // The first call on each device looks up the array's device address (the
 // set-up step); make that first call before capturing the stream into a CUDA
 // graph.  The array below is reserved on every GPU that loads the library, for
-// the life of the process (8 MiB).  It holds the inverse key norms of k1 and k2,
+// the life of the process (8.5 MiB).  It holds the inverse key norms of k1 and k2,
 // so it limits batch_heads * round_up(seq_len, 128) to kNoAllocMaxRows.
 //
 // All calls share the one array and it keeps whatever the last call wrote.
@@ -32,9 +32,11 @@
 namespace {
 
 constexpr long long kNoAllocMaxRows = 1ll << 20;  // per key tensor: batch_heads * padded seq_len
+constexpr long long kTableFloats = kNoAllocMaxRows / 16 * 17;  // key table of one key tensor
 
-// Inverse norms of k1 (first half) and k2 (second half).
-static __device__ __align__(256) float g_noalloc_scratch[2 * kNoAllocMaxRows];
+// Key tables (inverse norms and their per-16-key maxima) of k1 (first half)
+// and k2 (second half).
+static __device__ __align__(256) float g_noalloc_scratch[2 * kTableFloats];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
@@ -82,7 +84,7 @@ extern "C" int tda_diff_fwd_noalloc(const void* q1, const void* q2, const void* 
     char msg[256];
     snprintf(msg, sizeof(msg),
              "tda_diff_fwd_noalloc: batch_heads * padded seq_len = %lld exceeds the static scratch limit of "
-             "%lld rows (8 MiB); use tda_diff_fwd with a caller workspace",
+             "%lld rows (8.5 MiB); use tda_diff_fwd with a caller workspace",
              rows, kNoAllocMaxRows);
     tda::set_last_error(msg);
     return TDA_ERR_INVALID;
@@ -91,7 +93,7 @@ extern "C" int tda_diff_fwd_noalloc(const void* q1, const void* q2, const void* 
   int rc = scratch_on_current_device(&scratch);
   if (rc != TDA_OK) return rc;
   float* rk1 = scratch;
-  float* rk2 = scratch + kNoAllocMaxRows;
+  float* rk2 = scratch + kTableFloats;
   if ((rc = tda_key_inv_norms(k1, dtype, batch_heads, seq_len, head_dim, rk1, stream)) != TDA_OK) return rc;
   if ((rc = tda_key_inv_norms(k2, dtype, batch_heads, seq_len, head_dim, rk2, stream)) != TDA_OK) return rc;
   return tda_diff_fwd_tc(q1, q2, k1, k2, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, lambda_param,

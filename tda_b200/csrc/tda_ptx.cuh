@@ -62,7 +62,7 @@ struct WaitCtl {
 // After 1 ms of waiting the status word is polled as well, so once one CTA of
 // a grid has given up the others stop within about a millisecond instead of
 // each running out its own timeout.
-__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& ctl, int code) {
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& ctl, int code) {
   const uint64_t t0 = global_timer_ns();
   uint32_t it = 0;
   while (true) {

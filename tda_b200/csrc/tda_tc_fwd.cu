@@ -33,9 +33,12 @@
 
 #include "tda_internal.h"
 #include "tda_ptx.cuh"
+#include "tda_transform.cuh"
 
 namespace tda {
 namespace {
+
+using namespace tc;
 
 constexpr int kTransformWG = 2;                    // transform warpgroups
 constexpr int kTransformWarps = 4 * kTransformWG;  // warps 2 .. 17
@@ -47,7 +50,6 @@ constexpr int kSmemBudget = 232448;  // 227 KB opt-in dynamic shared memory
 constexpr int ST_PROD_SLOT = 0x101, ST_PROD_RK = 0x102;
 constexpr int ST_MMA_Q = 0x201, ST_MMA_SLOT = 0x202, ST_MMA_P = 0x203;
 constexpr int ST_TR_Q = 0x301, ST_TR_RK = 0x302, ST_TR_S = 0x303, ST_TR_O = 0x304;
-constexpr int ST_DRAIN = 0x401;
 
 template <int D, bool DIFF>
 struct Cfg {
@@ -55,7 +57,7 @@ struct Cfg {
   static constexpr int kBoxBytes = kTile * 128;  // 128 rows x 64 bf16 (128 B)
   static constexpr int kTileBytes = kTile * D * 2;
   static constexpr int kNQ = DIFF ? 2 : 1;
-  static constexpr int kRkPerTile = (DIFF ? 2 : 1) * kTile;
+  static constexpr int kRkPerTile = (DIFF ? 2 : 1) * (kTile + 8);  // rk then per-16-key maxima
   static constexpr int kRkFloats = kRkRing * kRkPerTile;
   static constexpr int kBarBytes = 1024;
   static constexpr int kFixed = kNQ * kTileBytes + kRkFloats * 4 + kBarBytes + 1024;
@@ -92,18 +94,6 @@ struct Bars {
   uint32_t tile_mask[2];
 };
 static_assert(sizeof(Bars) <= 1024, "barrier block too large");
-
-// Drain-time wait: ignores the abort flag, bounded by its own timeout.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, const WaitCtl& ctl) {
-  const uint32_t a = smem_u32(bar);
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(a, parity)) {
-    if (global_timer_ns() - t0 > ctl.timeout_ns) {
-      atomicCAS(ctl.status, 0, ST_DRAIN);
-      return;
-    }
-  }
-}
 
 // ------------------------------------------------------------------ producer
 template <int D, bool DIFF, bool NORM>
@@ -153,9 +143,14 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
       }
       mbar_arrive_expect_tx(&bars->rk_full[e], C::kRkPerTile * 4);
       float* dst = rk_s + e * C::kRkPerTile;
+      constexpr int kNB = DIFF ? 2 : 1;
       const size_t off = static_cast<size_t>(bh) * p.S_pad + static_cast<size_t>(j) * kTile;
+      const size_t moff = static_cast<size_t>(p.BH) * p.S_pad + static_cast<size_t>(bh) * (p.S_pad / 16) +
+                          static_cast<size_t>(j) * (kTile / 16);
       bulk_load(dst, p.rk1 + off, kTile * 4, &bars->rk_full[e]);
       if constexpr (DIFF) bulk_load(dst + kTile, p.rk2 + off, kTile * 4, &bars->rk_full[e]);
+      bulk_load(dst + kNB * kTile, p.rk1 + moff, 32, &bars->rk_full[e]);
+      if constexpr (DIFF) bulk_load(dst + kNB * kTile + 8, p.rk2 + moff, 32, &bars->rk_full[e]);
       ++rk_n;
     }
   };
@@ -320,152 +315,17 @@ __device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t 
   }
 }
 
-// ------------------------------------------------------------------ transform
-// Per-row coefficients: z = (s * rk_j - tq) * rq for each branch.  With
-// normalize, tq = tau * m and rq = 1 / m, m = max(||q_i||, 1e-12), so z is the
-// normalized score minus tau.  For p in {1, 2, 3} the differential weight is
-// folded into the second branch, rq2 *= lambda^(1/p), because
-// relu(c z)^p = c^p relu(z)^p for c >= 0; the general power keeps an explicit
-// lambda multiply.
-struct RowCoef {
-  float tq1, rq1, tq2, rq2;
-};
-
-__device__ __forceinline__ float2 f2u(uint32_t x, uint32_t y) {
-  return make_float2(__uint_as_float(x), __uint_as_float(y));
-}
-
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-__device__ __forceinline__ float2 relu2(float2 z) { return make_float2(fmaxf(z.x, 0.0f), fmaxf(z.y, 0.0f)); }
-
-template <int PM>
-__device__ __forceinline__ float2 relu_pow2(float2 z, float p) {
-  const float2 u = relu2(z);
-  if constexpr (PM == POW_1) {
-    return u;
-  } else if constexpr (PM == POW_2) {
-    return __fmul2_rn(u, u);
-  } else if constexpr (PM == POW_3) {
-    return __fmul2_rn(__fmul2_rn(u, u), u);
-  } else {
-    // exp(p * log(x + 1e-10)) for x > 0 (triton_threshold_attention.py:97-101)
-    return make_float2(u.x > 0.0f ? fast_ex2(p * fast_lg2(u.x + 1e-10f)) : 0.0f,
-                       u.y > 0.0f ? fast_ex2(p * fast_lg2(u.y + 1e-10f)) : 0.0f);
-  }
-}
-
-// One 32-key chunk of one row, from registers (a = S1, b = S2 as loaded from
-// TMEM) to P written over S1 in TMEM as bf16 hi (columns [0,16)) and lo
-// ([16,32)).  First pass computes y = s * rk - tq for every entry and its max;
-// P is nonzero only where y > 0, so when no lane of the warp has a positive y
-// the chunk is written as zeros without the power / combine / split work
-// (exact, and the common case for the sparse threshold maps TDA produces).
-// Returns this lane's 2-bit mask of 16-key halves holding a nonzero P.
-template <int PM, bool DIFF, bool NORM, bool MASK>
-__device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t (&b)[32], uint32_t s1_addr,
-                                                    const float* rk1, const float* rk2, int limit, const RowCoef& c,
-                                                    float relu_power, float lam) {
-  constexpr bool kFold = PM != POW_GENERAL;
-  float mx[2] = {-3.0e38f, -3.0e38f};  // max y over keys [0,16) and [16,32)
-#pragma unroll
-  for (int e4 = 0; e4 < 8; ++e4) {
-    float4 r1 = make_float4(1.f, 1.f, 1.f, 1.f), r2 = r1;
-    if constexpr (NORM) {
-      r1 = *reinterpret_cast<const float4*>(rk1 + 4 * e4);
-      if constexpr (DIFF) r2 = *reinterpret_cast<const float4*>(rk2 + 4 * e4);
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int i = 4 * e4 + 2 * h;
-      uint32_t x0 = a[i], x1 = a[i + 1];
-      if constexpr (MASK) {
-        x0 = (i <= limit) ? x0 : 0u;
-        x1 = (i + 1 <= limit) ? x1 : 0u;
-      }
-      const float2 rr = h ? make_float2(r1.z, r1.w) : make_float2(r1.x, r1.y);
-      const float2 y = NORM ? __ffma2_rn(f2u(x0, x1), rr, make_float2(-c.tq1, -c.tq1))
-                            : __fadd2_rn(f2u(x0, x1), make_float2(-c.tq1, -c.tq1));
-      a[i] = __float_as_uint(y.x);
-      a[i + 1] = __float_as_uint(y.y);
-      mx[e4 >> 2] = max3f(mx[e4 >> 2], y.x, y.y);
-      if constexpr (DIFF) {
-        uint32_t w0 = b[i], w1 = b[i + 1];
-        if constexpr (MASK) {
-          w0 = (i <= limit) ? w0 : 0u;
-          w1 = (i + 1 <= limit) ? w1 : 0u;
-        }
-        const float2 rs = h ? make_float2(r2.z, r2.w) : make_float2(r2.x, r2.y);
-        const float2 y2 = NORM ? __ffma2_rn(f2u(w0, w1), rs, make_float2(-c.tq2, -c.tq2))
-                               : __fadd2_rn(f2u(w0, w1), make_float2(-c.tq2, -c.tq2));
-        b[i] = __float_as_uint(y2.x);
-        b[i + 1] = __float_as_uint(y2.y);
-        mx[e4 >> 2] = max3f(mx[e4 >> 2], y2.x, y2.y);
-      }
-    }
-  }
-  const uint32_t nz = (mx[0] > 0.0f ? 1u : 0u) | (mx[1] > 0.0f ? 2u : 0u);
-  if (__any_sync(0xffffffffu, nz != 0u)) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t hi[8], lo[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int e2 = 8 * half + q;
-        const float2 y1 = f2u(a[2 * e2], a[2 * e2 + 1]);
-        const float2 z1 = NORM ? __fmul2_rn(y1, make_float2(c.rq1, c.rq1)) : y1;
-        float2 P;
-        if constexpr (DIFF) {
-          const float2 y2 = f2u(b[2 * e2], b[2 * e2 + 1]);
-          const float2 z2 = (NORM || kFold) ? __fmul2_rn(y2, make_float2(c.rq2, c.rq2)) : y2;
-          if constexpr (PM == POW_2) {
-            const float2 u1 = relu2(z1), u2 = relu2(z2);
-            P = __ffma2_rn(u1, u1, __fmul2_rn(u2, make_float2(-u2.x, -u2.y)));
-          } else if constexpr (kFold) {
-            const float2 p2 = relu_pow2<PM>(z2, relu_power);
-            P = __fadd2_rn(relu_pow2<PM>(z1, relu_power), make_float2(-p2.x, -p2.y));
-          } else {
-            P = __ffma2_rn(make_float2(-lam, -lam), relu_pow2<PM>(z2, relu_power),
-                           relu_pow2<PM>(z1, relu_power));
-          }
-        } else {
-          P = relu_pow2<PM>(z1, relu_power);
-        }
-        // hi = P truncated to bf16 (exact in fp32), lo = bf16(P - hi): hi + lo
-        // carries ~16 significant bits of P.
-        const uint32_t p0 = __float_as_uint(P.x), p1 = __float_as_uint(P.y);
-        hi[q] = __byte_perm(p0, p1, 0x7632);
-        const float2 l = __fadd2_rn(P, make_float2(-__uint_as_float(p0 & 0xFFFF0000u),
-                                                   -__uint_as_float(p1 & 0xFFFF0000u)));
-        lo[q] = pack_bf16x2(l.x, l.y);
-      }
-      tmem_st8(s1_addr + 8 * half, hi);
-      tmem_st8(s1_addr + 16 + 8 * half, lo);
-    }
-  } else {
-    const uint32_t zero[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    tmem_st8(s1_addr, zero);
-    tmem_st8(s1_addr + 8, zero);
-    tmem_st8(s1_addr + 16, zero);
-    tmem_st8(s1_addr + 24, zero);
-  }
-  return nz;
-}
-
 // Transform warps: warp w (2 <= w < 2 + kTransformWarps) owns TMEM lane
 // quarter w % 4 (query rows) and, as warpgroup g = (w - 2) / 4, the key
 // chunks [g kChunks, (g+1) kChunks) of every key tile (32 keys each) and the
 // output columns [g D/kTransformWG, (g+1) D/kTransformWG).
-template <int D, bool DIFF, bool NORM, int PM>
+template <int D, bool DIFF, bool NORM, bool POS, int PM>
 __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem,
                               int bh, int qt, int n_kt, int warp, int lane) {
   using C = Cfg<D, DIFF>;
   constexpr bool kFold = PM != POW_GENERAL;
   constexpr int kChunks = 4 / kTransformWG;  // 32-key chunks per thread per tile
+  static_assert(kChunks == 2, "transform_tile handles two chunks");
   const int wg = (warp - 2) >> 2;
   const int quarter = warp & 3;
   const int row = quarter * 32 + lane;
@@ -525,38 +385,15 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     if (!ok) break;
     tc_fence_after();
     const uint32_t s1col = DIFF ? ((j & 1) ? 256u : 0u) : static_cast<uint32_t>((j & 1) * 128);
-    // all of this thread's S (and S2) columns in one round of TMEM loads
-    uint32_t a[kChunks][32];
-    uint32_t b[kChunks][32];
-#pragma unroll
-    for (int cc = 0; cc < kChunks; ++cc) {
-      const int ch = wg * kChunks + cc;
-      tmem_ld32(tmem + lane_off + s1col + 32 * ch, a[cc]);
-      if constexpr (DIFF) tmem_ld32(tmem + lane_off + C::kColS2 + 32 * ch, b[cc]);
-    }
-    tmem_wait_ld();
-    if constexpr (DIFF) {
-      // S2 is in registers: hand its TMEM slot back so QK2 of the next tile
-      // runs on the tensor cores while this tile is transformed
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->s2_free[j & 1]);
-    }
-    uint32_t nz = 0;  // bit (2 cc + h): 16-key half h of chunk cc has a nonzero P
-#pragma unroll
-    for (int cc = 0; cc < kChunks; ++cc) {
-      const int ch = wg * kChunks + cc;
-      const uint32_t s1 = tmem + lane_off + s1col + 32 * ch;
-      const float* r1 = rk_s + re * C::kRkPerTile + 32 * ch;
-      const float* r2 = r1 + kTile;
-      const int limit = grow - (j * kTile + 32 * ch);
-      if (j >= qt)  // tile overlaps the causal diagonal
-        nz |= transform_chunk<PM, DIFF, NORM, true>(a[cc], b[cc], s1, r1, r2, limit, c, p.relu_power, p.lam)
-              << (2 * cc);
-      else
-        nz |= transform_chunk<PM, DIFF, NORM, false>(a[cc], b[cc], s1, r1, r2, limit, c, p.relu_power, p.lam)
-              << (2 * cc);
-    }
+    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS>(
+        tmem + lane_off, s1col, C::kColS2, wg, rk_s + re * C::kRkPerTile, grow - j * kTile, j >= qt, c,
+        p.relu_power, p.lam, [&] {
+          // S2 is in registers: hand its TMEM slot back so QK2 of the next
+          // tile runs on the tensor cores while this tile is transformed
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->s2_free[j & 1]);
+        });
     // publish which 16-key slabs of this tile hold a nonzero P (this
     // warpgroup owns slabs [2 kChunks wg, 2 kChunks (wg + 1))); slabs nobody
     // marks are skipped by the PV.  The p_full arrive below orders the store
@@ -618,7 +455,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
   }
 }
 
-template <int D, bool DIFF, bool NORM, int PM>
+template <int D, bool DIFF, bool NORM, bool POS, int PM>
 __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
   using C = Cfg<D, DIFF>;
   extern __shared__ uint8_t smem_raw[];
@@ -683,7 +520,7 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
     if (lane == 0) run_mma<D, DIFF>(smem, bars, ctl, tmem, n_kt);
     __syncwarp();
   } else {
-    run_transform<D, DIFF, NORM, PM>(p, smem, bars, ctl, tmem, bh, qt, n_kt, warp, lane);
+    run_transform<D, DIFF, NORM, POS, PM>(p, smem, bars, ctl, tmem, bh, qt, n_kt, warp, lane);
   }
 
   tc_fence_before();
@@ -694,10 +531,10 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
   }
 }
 
-template <int D, bool DIFF, bool NORM, int PM>
+template <int D, bool DIFF, bool NORM, bool POS, int PM>
 cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
   using C = Cfg<D, DIFF>;
-  auto kern = tda_tc_fwd_kernel<D, DIFF, NORM, PM>;
+  auto kern = tda_tc_fwd_kernel<D, DIFF, NORM, POS, PM>;
   static bool attr_done = false;  // per instantiation; attribute is per-function, idempotent
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
@@ -722,19 +559,23 @@ cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
   return e;
 }
 
-template <int D, bool DIFF, bool NORM>
+template <int D, bool DIFF, bool NORM, bool POS>
 cudaError_t dispatch_pow(const TcFwdParams& p, int pm, cudaStream_t s) {
   switch (pm) {
-    case POW_1: return launch_one<D, DIFF, NORM, POW_1>(p, s);
-    case POW_2: return launch_one<D, DIFF, NORM, POW_2>(p, s);
-    case POW_3: return launch_one<D, DIFF, NORM, POW_3>(p, s);
-    default: return launch_one<D, DIFF, NORM, POW_GENERAL>(p, s);
+    case POW_1: return launch_one<D, DIFF, NORM, POS, POW_1>(p, s);
+    case POW_2: return launch_one<D, DIFF, NORM, POS, POW_2>(p, s);
+    case POW_3: return launch_one<D, DIFF, NORM, POS, POW_3>(p, s);
+    default: return launch_one<D, DIFF, NORM, POS, POW_GENERAL>(p, s);
   }
 }
 
+// beta >= 0 (tau >= 0): zero halves are recognised from the raw scores, and
+// with normalize the ReLU is a saturating multiply
 template <int D, bool DIFF>
 cudaError_t dispatch_norm(const TcFwdParams& p, bool norm, int pm, cudaStream_t s) {
-  return norm ? dispatch_pow<D, DIFF, true>(p, pm, s) : dispatch_pow<D, DIFF, false>(p, pm, s);
+  if (norm)
+    return p.causal_skip ? dispatch_pow<D, DIFF, true, true>(p, pm, s) : dispatch_pow<D, DIFF, true, false>(p, pm, s);
+  return p.causal_skip ? dispatch_pow<D, DIFF, false, true>(p, pm, s) : dispatch_pow<D, DIFF, false, false>(p, pm, s);
 }
 
 template <int D>

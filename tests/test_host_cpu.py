@@ -39,9 +39,10 @@ def test_library_exports_every_declared_symbol():
 def test_library_host_only_calls():
     lib = _lib.load()
     assert lib.tda_version() == 100
-    # workspace: per-key inverse norms, 128-row padded, 256-B aligned per tensor
-    assert lib.tda_workspace_size(0, _lib.TDA_BF16, 2, 100, 64, 1) == 1024
-    assert lib.tda_workspace_size(1, _lib.TDA_BF16, 2, 100, 64, 1) == 2048
+    # workspace: per key tensor a key table of 2 x 128 (padded rows) x 17/16
+    # floats = 1088 B, rounded up to 256 B
+    assert lib.tda_workspace_size(0, _lib.TDA_BF16, 2, 100, 64, 1) == 1280
+    assert lib.tda_workspace_size(1, _lib.TDA_BF16, 2, 100, 64, 1) == 2560
     assert lib.tda_workspace_size(1, _lib.TDA_BF16, 2, 100, 64, 0) == 0
     assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 64, 1) == 0
 
