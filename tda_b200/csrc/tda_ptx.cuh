@@ -241,6 +241,23 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool ab_bf16, boo
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
+// Named barrier `id` over `nthreads` threads (a multiple of 32) that also
+// ANDs a predicate across them: every participating thread must arrive once,
+// whatever its own predicate, so a thread that gave up on an earlier wait
+// still releases the others.  Orders shared-memory accesses like bar.sync.
+__device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ---------------------------------------------------------------- misc
 // Pack two floats to bf16x2 (round to nearest even); `lo` goes in bits 0-15.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -14,13 +14,18 @@
 //   warp 0      TMA producer: Q tile(s) once, then a ring of K/V tiles in the
 //               exact order the MMA warp consumes them, plus the per-key
 //               inverse norms into a small ring.
-//   warp 1      MMA issuer (one thread): S = Q K^T into TMEM (SS form), and
-//               O += P V with P read from TMEM (TS form).
+//   warp 1      MMA issuer (one thread): S = Q K^T (S1 = Q1 K1^T) into TMEM
+//               (SS form), and O += P V with P read from TMEM (TS form).
 //   warps 2-9   two transform warpgroups; each thread owns one query row
 //               (its TMEM lane), warpgroup g handles key columns [64g, 64g+64)
 //               of every tile: S -> threshold -> ReLU^p (-> combine) ->
 //               bf16 hi + bf16 lo split of P written back over S in TMEM.
 //               They also run the epilogue (O from TMEM -> global).
+//   warp 10     differential form only: second MMA issuer for S2 = Q2 K2^T.
+//               An issuing thread blocks while the tensor pipe's queue is
+//               full, so one issuer for everything would see the S2 slot
+//               freed only after its PV and QK1 products went in, and the
+//               pipe would idle in between.
 //
 // P precision: P is stored as bf16 hi + bf16 lo (P = hi + lo to ~16 bits) and
 // multiplied into O by two MMAs; a single bf16 P misses the 1e-3 accuracy gate.
@@ -41,14 +46,18 @@ namespace {
 using namespace tc;
 
 constexpr int kTransformWG = 2;                    // transform warpgroups
-constexpr int kTransformWarps = 4 * kTransformWG;  // warps 2 .. 17
-constexpr int kThreads = 32 * (2 + kTransformWarps);
+constexpr int kTransformWarps = 4 * kTransformWG;  // warps 2 .. 9
+// differential form: warp 10 issues the QK2 products (second MMA issuer)
+constexpr int kQk2Warp = 2 + kTransformWarps;
+template <bool DIFF>
+constexpr int threads_for() { return 32 * (2 + kTransformWarps + (DIFF ? 1 : 0)); }
 constexpr int kRkRing = 4;
+constexpr int kHeadGroup = 4;  // (batch, head) slices interleaved in launch order
 constexpr int kSmemBudget = 232448;  // 227 KB opt-in dynamic shared memory
 
 // status codes (role << 8 | site)
 constexpr int ST_PROD_SLOT = 0x101, ST_PROD_RK = 0x102;
-constexpr int ST_MMA_Q = 0x201, ST_MMA_SLOT = 0x202, ST_MMA_P = 0x203;
+constexpr int ST_MMA_Q = 0x201, ST_MMA_SLOT = 0x202, ST_MMA_P = 0x203, ST_MMA_S2 = 0x204;
 constexpr int ST_TR_Q = 0x301, ST_TR_RK = 0x302, ST_TR_S = 0x303, ST_TR_O = 0x304;
 
 template <int D, bool DIFF>
@@ -60,18 +69,24 @@ struct Cfg {
   static constexpr int kRkPerTile = (DIFF ? 2 : 1) * (kTile + 8);  // rk then per-16-key maxima
   static constexpr int kRkFloats = kRkRing * kRkPerTile;
   static constexpr int kBarBytes = 1024;
-  static constexpr int kFixed = kNQ * kTileBytes + kRkFloats * 4 + kBarBytes + 1024;
+  static constexpr int kQssBytes = kNQ * kTransformWG * kTile * 4;  // partial sums of ||q||^2
+  static constexpr int kFixed = kNQ * kTileBytes + kRkFloats * 4 + kBarBytes + kQssBytes + 1024;
   static constexpr int kSlotsRaw = (kSmemBudget - kFixed) / kTileBytes;
   static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
   static_assert(kSlots >= 3, "not enough shared memory for the K/V ring");
   static constexpr int kOffRing = kNQ * kTileBytes;
   static constexpr int kOffRk = kOffRing + kSlots * kTileBytes;
   static constexpr int kOffBar = kOffRk + kRkFloats * 4;
-  static constexpr int kSmemBytes = kOffBar + kBarBytes + 1024;
-  // TMEM columns (512 allocated): rect S slots {0,128}, O at 256;
+  static constexpr int kOffQss = kOffBar + kBarBytes;
+  static constexpr int kSmemBytes = kOffQss + kQssBytes + 1024;
+  // TMEM columns (512 allocated): rect S slots {0,128,256}, O at 384;
   // diff S1 slots {0,256}, S2 slot 128, O at 384.
+  static constexpr int kSSlots = DIFF ? 2 : 3;
   static constexpr int kColS2 = 128;
-  static constexpr int kColO = DIFF ? 384 : 256;
+  static constexpr int kColO = 384;
+  static __device__ __forceinline__ uint32_t col_s(int slot) {
+    return DIFF ? (slot ? 256u : 0u) : static_cast<uint32_t>(slot * 128);
+  }
   static constexpr uint32_t kIdescQK = idesc_f16(128, 128, true, false);
   static constexpr uint32_t kIdescPV = idesc_f16(128, D, true, true);
 };
@@ -80,8 +95,9 @@ struct Bars {
   uint64_t q_full;
   uint64_t o_full;
   uint64_t drain;
-  uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t drain2;      // differential: the QK2 issuer's own MMAs
+  uint64_t s_full[3];   // per S slot; differential: one arrival per MMA issuer
+  uint64_t p_full[3];
   uint64_t s2_free[2];  // differential: every transform warp has read S2 of the tile
   uint64_t rk_full[kRkRing];
   uint64_t rk_empty[kRkRing];
@@ -89,9 +105,9 @@ struct Bars {
   uint64_t slot_empty[8];
   uint32_t tmem_base;
   int abort_flag;
-  // per key tile (by parity): (j + 1) << 8 | mask of 16-key slabs with a
+  // per S slot: (j + 1) << 8 | mask of 16-key slabs of key tile j with a
   // nonzero P; stale words carry an older tag and read as mask 0
-  uint32_t tile_mask[2];
+  uint32_t tile_mask[3];
 };
 static_assert(sizeof(Bars) <= 1024, "barrier block too large");
 
@@ -156,18 +172,16 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
   };
 
   if constexpr (!DIFF) {
-    // consumption order: K0, K1, then per j: V_j, K_{j+2}
-    load_rk(0);
-    load_tile(&p.tm_k1, 0);
-    if (n_kt > 1) {
-      load_rk(1);
-      load_tile(&p.tm_k1, 1);
+    // consumption order: K0, K1, K2, then per j: V_j, K_{j+3}
+    for (int j = 0; j < 3 && j < n_kt; ++j) {
+      load_rk(j);
+      load_tile(&p.tm_k1, j);
     }
     for (int j = 0; j < n_kt && ok; ++j) {
       load_tile(&p.tm_v, j);
-      if (j + 2 < n_kt) {
-        load_rk(j + 2);
-        load_tile(&p.tm_k1, j + 2);
+      if (j + 3 < n_kt) {
+        load_rk(j + 3);
+        load_tile(&p.tm_k1, j + 3);
       }
     }
   } else {
@@ -200,29 +214,38 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
   }
 }
 
-// ------------------------------------------------------------------ MMA issuer
-template <int D, bool DIFF>
-__device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
-  using C = Cfg<D, DIFF>;
-  const uint32_t q1_base = smem_u32(smem);
-  const uint32_t q2_base = q1_base + C::kTileBytes;
-  const uint32_t ring_base = smem_u32(smem + C::kOffRing);
-  bool ok = mbar_wait(&bars->q_full, 0, ctl, ST_MMA_Q);
-  tc_fence_after();
-  int ridx = 0;
+// ------------------------------------------------------------------ MMA issuers
+// Position of a tile in the producer's ring order (differential form):
+//   K1_0, K2_0, K1_1, then per key tile j: K2_{j+1}, V_j, K1_{j+2}
+// (entries past the last tile are not loaded).
+__device__ __forceinline__ int ring_k1(int m) { return m == 0 ? 0 : (m == 1 ? 2 : 3 * m - 1); }
+__device__ __forceinline__ int ring_k2(int m) { return m == 0 ? 1 : 3 * m; }
+__device__ __forceinline__ int ring_v(int j, int n_kt) { return j <= n_kt - 2 ? 4 + 3 * j : 3 * n_kt - 1; }
 
-  auto acquire = [&](int& slot) {
-    slot = ridx % C::kSlots;
-    const uint32_t par = (ridx / C::kSlots) & 1;
-    ++ridx;
-    if (!ok) return;
-    ok = mbar_wait(&bars->slot_full[slot], par, ctl, ST_MMA_SLOT);
+template <int D, bool DIFF>
+struct MmaIssuer {
+  using C = Cfg<D, DIFF>;
+  Bars* bars;
+  const WaitCtl& ctl;
+  uint32_t tmem;
+  uint32_t ring_base;
+  bool ok;
+  bool o_started;
+
+  __device__ MmaIssuer(uint8_t* smem, Bars* b, const WaitCtl& c, uint32_t t)
+      : bars(b), ctl(c), tmem(t), ring_base(smem_u32(smem + C::kOffRing)), ok(true), o_started(false) {}
+
+  // wait for ring entry `idx` to land; returns its slot
+  __device__ int acquire(int idx) {
+    const int slot = idx % C::kSlots;
+    if (!ok) return slot;
+    ok = mbar_wait(&bars->slot_full[slot], (idx / C::kSlots) & 1, ctl, ST_MMA_SLOT);
     tc_fence_after();
-  };
-  // S[dcol] = Q K^T over D in UMMA_K = 16 steps (32 B inside a 128-B swizzled row).
-  auto qk = [&](uint32_t dcol, uint32_t q_base) {
-    int slot;
-    acquire(slot);
+    return slot;
+  }
+  // S[dcol] = Q K^T over D in UMMA_K = 16 steps (32 B inside a 128-B swizzled row)
+  __device__ void qk(int idx, uint32_t dcol, uint32_t q_base) {
+    const int slot = acquire(idx);
     if (!ok) return;
     const uint32_t k_base = ring_base + slot * C::kTileBytes;
 #pragma unroll
@@ -232,16 +255,14 @@ __device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t 
              C::kIdescQK, kk > 0 ? 1u : 0u);
     }
     tc_commit(&bars->slot_empty[slot]);
-  };
+  }
   // O += P V, P (hi, lo) in TMEM columns [pcol, pcol+128): for key chunk c of
   // 32 keys, hi at pcol + 32c + [0,16), lo at pcol + 32c + [16,32).  Only the
   // 16-key slabs set in `mask` are multiplied (the others hold P = 0); the
   // first PV of the CTA initialises O (accumulate = 0) and therefore always
   // issues at least its first slab.
-  bool o_started = false;
-  auto pv = [&](uint32_t pcol, uint32_t mask) {
-    int slot;
-    acquire(slot);
+  __device__ void pv(int idx, uint32_t pcol, uint32_t mask) {
+    const int slot = acquire(idx);
     if (!ok) return;
     if (!o_started) mask |= 1u;
     if (mask == 0u) {
@@ -259,60 +280,93 @@ __device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t 
       o_started = true;
     }
     tc_commit(&bars->slot_empty[slot]);
-  };
-  auto slab_mask = [&](int j) -> uint32_t {
-    const uint32_t w = *reinterpret_cast<volatile uint32_t*>(&bars->tile_mask[j & 1]);
+  }
+  __device__ uint32_t slab_mask(int j) const {
+    const uint32_t w = *reinterpret_cast<volatile uint32_t*>(&bars->tile_mask[j % C::kSSlots]);
     return (w >> 8) == static_cast<uint32_t>(j + 1) ? (w & 0xFFu) : 0u;
-  };
-  auto wait_p = [&](int j) {
+  }
+  __device__ void wait(uint64_t* bar, uint32_t parity, int code) {
     if (!ok) return;
-    ok = mbar_wait(&bars->p_full[j & 1], (j >> 1) & 1, ctl, ST_MMA_P);
+    ok = mbar_wait(bar, parity, ctl, code);
     tc_fence_after();
-  };
+  }
+  __device__ void commit(uint64_t* bar) {
+    if (ok) tc_commit(bar);
+  }
+  // Abort: let every MMA this thread issued finish before TMEM is freed.
+  __device__ void drain(uint64_t* bar) {
+    tc_commit(bar);
+    drain_wait(bar, 0, ctl);
+  }
+};
 
+// Main issuer (warp 1): QK (rect) or QK1 (differential) and every PV.
+// rect: three S slots; QK_{j+3} reuses the slot of P_j right after PV_j
+// (the tensor pipe runs one thread's MMAs in order).
+// differential: two S1 slots; the QK2 products come from warp 10.
+template <int D, bool DIFF>
+__device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
+  using C = Cfg<D, DIFF>;
+  MmaIssuer<D, DIFF> m(smem, bars, ctl, tmem);
+  const uint32_t q1_base = smem_u32(smem);
+  m.wait(&bars->q_full, 0, ST_MMA_Q);
   if constexpr (!DIFF) {
-    qk(0, q1_base);
-    if (ok) tc_commit(&bars->s_full[0]);
+    int ridx = 0;  // ring order: K0, K1, K2, then per j: V_j, K_{j+3}
+    for (int t = 0; t < C::kSSlots && t < n_kt; ++t) {
+      m.qk(ridx++, C::col_s(t), q1_base);
+      m.commit(&bars->s_full[t]);
+    }
+    for (int j = 0; j < n_kt && m.ok; ++j) {
+      const int slot = j % C::kSSlots;
+      m.wait(&bars->p_full[slot], (j / C::kSSlots) & 1, ST_MMA_P);
+      m.pv(ridx++, C::col_s(slot), m.slab_mask(j));
+      if (j + C::kSSlots < n_kt) {
+        m.qk(ridx++, C::col_s(slot), q1_base);
+        m.commit(&bars->s_full[slot]);
+      }
+    }
+  } else {
+    m.qk(ring_k1(0), C::col_s(0), q1_base);
+    m.commit(&bars->s_full[0]);
     if (n_kt > 1) {
-      qk(128, q1_base);
-      if (ok) tc_commit(&bars->s_full[1]);
+      m.qk(ring_k1(1), C::col_s(1), q1_base);
+      m.commit(&bars->s_full[1]);
     }
-    for (int j = 0; j < n_kt && ok; ++j) {
-      const uint32_t col = (j & 1) * 128;
-      wait_p(j);
-      pv(col, slab_mask(j));
+    for (int j = 0; j < n_kt && m.ok; ++j) {
+      const int slot = j & 1;
+      m.wait(&bars->p_full[slot], (j >> 1) & 1, ST_MMA_P);
+      m.pv(ring_v(j, n_kt), C::col_s(slot), m.slab_mask(j));
       if (j + 2 < n_kt) {
-        qk(col, q1_base);
-        if (ok) tc_commit(&bars->s_full[j & 1]);
+        m.qk(ring_k1(j + 2), C::col_s(slot), q1_base);
+        m.commit(&bars->s_full[slot]);
       }
-    }
-  } else {
-    qk(0, q1_base);
-    qk(C::kColS2, q2_base);
-    if (ok) tc_commit(&bars->s_full[0]);
-    if (n_kt > 1) qk(256, q1_base);
-    for (int j = 0; j < n_kt && ok; ++j) {
-      const uint32_t col = (j & 1) ? 256 : 0;
-      if (j + 1 < n_kt) {
-        // S2 has one TMEM slot: it is free once every transform warp holds
-        // S2_j in registers, long before P_j is ready
-        ok = mbar_wait(&bars->s2_free[j & 1], (j >> 1) & 1, ctl, ST_MMA_P);
-        tc_fence_after();
-        qk(C::kColS2, q2_base);
-        if (ok) tc_commit(&bars->s_full[(j + 1) & 1]);
-      }
-      wait_p(j);
-      pv(col, slab_mask(j));
-      if (j + 2 < n_kt) qk(col, q1_base);
     }
   }
-  if (ok) {
+  if (m.ok)
     tc_commit(&bars->o_full);
-  } else {
-    // Abort: let every MMA already issued finish before TMEM is freed.
-    tc_commit(&bars->drain);
-    drain_wait(&bars->drain, 0, ctl);
+  else
+    m.drain(&bars->drain);
+}
+
+// Second issuer of the differential form (warp 10): S2 = Q2 K2^T into its
+// single TMEM slot.  The slot is free once every transform warp holds S2_j in
+// registers (s2_free), which happens long before P_j is ready; a separate
+// thread issues these products so that the main issuer, blocked while the
+// tensor pipe accepts its PV and QK1 products, does not delay them.
+template <int D>
+__device__ void run_mma_qk2(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
+  using C = Cfg<D, true>;
+  MmaIssuer<D, true> m(smem, bars, ctl, tmem);
+  const uint32_t q2_base = smem_u32(smem) + C::kTileBytes;
+  m.wait(&bars->q_full, 0, ST_MMA_Q);
+  m.qk(ring_k2(0), C::kColS2, q2_base);
+  m.commit(&bars->s_full[0]);
+  for (int j = 0; j + 1 < n_kt && m.ok; ++j) {
+    m.wait(&bars->s2_free[j & 1], (j >> 1) & 1, ST_MMA_S2);
+    m.qk(ring_k2(j + 1), C::kColS2, q2_base);
+    m.commit(&bars->s_full[(j + 1) & 1]);
   }
+  if (!m.ok) m.drain(&bars->drain2);
 }
 
 // Transform warps: warp w (2 <= w < 2 + kTransformWarps) owns TMEM lane
@@ -341,34 +395,43 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
   bool ok = true;
   if constexpr (NORM) {
     ok = mbar_wait_warp(&bars->q_full, 0, ctl, ST_TR_Q);
+    // ||q_i|| from the swizzled tile(s): row r's 16-B chunks are permuted
+    // within the row only, so summing chunks needs no unswizzle.  The two
+    // warpgroups (which own the same rows) each sum half of every row's
+    // chunks and exchange the partial sums through shared memory.  A rolled
+    // loop keeps this once-per-CTA code small in the instruction cache.
+    float* qss = reinterpret_cast<float*>(smem + C::kOffQss);  // [kNQ][kTransformWG][kTile]
     if (ok) {
-      // ||q_i|| from the swizzled tile: row r's 16-B chunks are permuted
-      // within the row only, so summing all chunks needs no unswizzle; the
-      // chunk visit order is rotated by (r & 7) to avoid bank conflicts.
-      float ss[2] = {0.f, 0.f};
-#pragma unroll
+#pragma unroll 1
       for (int t = 0; t < C::kNQ; ++t) {
-        const uint8_t* qb = smem + t * C::kTileBytes + row * 128;
-#pragma unroll
+        float ss = 0.0f;
+#pragma unroll 1
         for (int bx = 0; bx < C::kBoxes; ++bx) {
+          const uint8_t* rb = smem + t * C::kTileBytes + bx * C::kBoxBytes + row * 128;
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            const uint4 u = *reinterpret_cast<const uint4*>(qb + bx * C::kBoxBytes + ((cc ^ (row & 7)) << 4));
+          for (int k = 0; k < 4; ++k) {
+            const int cc = 4 * wg + ((k + row) & 3);  // rotated start: fewer bank conflicts
+            const uint4 u = *reinterpret_cast<const uint4*>(rb + ((cc ^ (row & 7)) << 4));
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
               const float lo = __uint_as_float(w[h] << 16), hi = __uint_as_float(w[h] & 0xFFFF0000u);
-              ss[t] = fmaf(lo, lo, ss[t]);
-              ss[t] = fmaf(hi, hi, ss[t]);
+              ss = fmaf(lo, lo, ss);
+              ss = fmaf(hi, hi, ss);
             }
           }
         }
+        qss[(t * kTransformWG + wg) * kTile + row] = ss;
       }
-      const float m1 = fmaxf(sqrtf(ss[0]), 1e-12f);
+    }
+    // every transform thread arrives, also one whose wait gave up
+    ok = named_barrier_and(1, 32 * kTransformWarps, ok);
+    if (ok) {
+      const float m1 = fmaxf(sqrtf(qss[row] + qss[kTile + row]), 1e-12f);
       c.rq1 = 1.0f / m1;
       c.tq1 = tau * m1;
       if constexpr (DIFF) {
-        const float m2 = fmaxf(sqrtf(ss[1]), 1e-12f);
+        const float m2 = fmaxf(sqrtf(qss[2 * kTile + row] + qss[3 * kTile + row]), 1e-12f);
         c.rq2 = lam2 / m2;
         c.tq2 = tau * m2;
       }
@@ -381,10 +444,12 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
       ok = mbar_wait_warp(&bars->rk_full[re], (j / kRkRing) & 1, ctl, ST_TR_RK);
       if (!ok) break;
     }
-    ok = mbar_wait_warp(&bars->s_full[j & 1], (j >> 1) & 1, ctl, ST_TR_S);
+    const int slot = j % C::kSSlots;
+    const uint32_t sphase = (j / C::kSSlots) & 1;
+    ok = mbar_wait_warp(&bars->s_full[slot], sphase, ctl, ST_TR_S);
     if (!ok) break;
     tc_fence_after();
-    const uint32_t s1col = DIFF ? ((j & 1) ? 256u : 0u) : static_cast<uint32_t>((j & 1) * 128);
+    const uint32_t s1col = C::col_s(slot);
     const uint32_t nz = transform_tile<PM, DIFF, NORM, POS>(
         tmem + lane_off, s1col, C::kColS2, wg, rk_s + re * C::kRkPerTile, grow - j * kTile, j >= qt, c,
         p.relu_power, p.lam, [&] {
@@ -400,7 +465,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     // before the MMA warp reads the word.
     const uint32_t wmask = __reduce_or_sync(0xffffffffu, nz) << (2 * kChunks * wg);
     if (wmask != 0u && lane == 0) {
-      uint32_t* word = &bars->tile_mask[j & 1];
+      uint32_t* word = &bars->tile_mask[slot];
       const uint32_t tag = static_cast<uint32_t>(j + 1) << 8;
       uint32_t old = *reinterpret_cast<volatile uint32_t*>(word), assumed;
       do {
@@ -415,7 +480,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     tc_fence_before();
     __syncwarp();
     if (lane == 0) {
-      mbar_arrive(&bars->p_full[j & 1]);
+      mbar_arrive(&bars->p_full[slot]);
       if constexpr (NORM) mbar_arrive(&bars->rk_empty[re]);
     }
   }
@@ -464,23 +529,32 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Head-major order, longest query tile first within a head: the CTAs in
-  // flight at any time cover only a few (batch, head) slices, so each K/V tile
-  // is read from HBM about once and then served from L2 to every query tile
-  // of that head.
-  const int bh = static_cast<int>(blockIdx.x / p.n_qtiles);
-  const int qt = p.n_qtiles - 1 - static_cast<int>(blockIdx.x % p.n_qtiles);
+  // Launch order: groups of kHeadGroup (batch, head) slices, and inside a
+  // group the query tiles longest first with the group's heads interleaved.
+  // The CTAs in flight at any time then cover only a few slices, so each K/V
+  // tile is read from HBM about once and served from L2 to every query tile
+  // of its head, and the causal work per CTA falls monotonically towards the
+  // end of each group (longest-processing-time-first: short tiles fill the
+  // SMs that free up while the long tiles of the group finish).
+  const int per_group = kHeadGroup * p.n_qtiles;
+  const int g0 = static_cast<int>(blockIdx.x / per_group) * kHeadGroup;
+  const int gsz = min(kHeadGroup, p.BH - g0);
+  const int r = static_cast<int>(blockIdx.x % per_group);
+  const int bh = g0 + r % gsz;
+  const int qt = p.n_qtiles - 1 - r / gsz;
   const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->q_full, 1);
     mbar_init(&bars->o_full, 1);
     mbar_init(&bars->drain, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->s_full[i], 1);
+    mbar_init(&bars->drain2, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->s_full[i], DIFF ? 2 : 1);
       mbar_init(&bars->p_full[i], kTransformWarps);
-      mbar_init(&bars->s2_free[i], kTransformWarps);
+      bars->tile_mask[i] = 0;
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->s2_free[i], kTransformWarps);
     for (int i = 0; i < kRkRing; ++i) {
       mbar_init(&bars->rk_full[i], 1);
       mbar_init(&bars->rk_empty[i], kTransformWarps);
@@ -490,8 +564,6 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
       mbar_init(&bars->slot_empty[i], 1);
     }
     bars->abort_flag = 0;
-    bars->tile_mask[0] = 0;
-    bars->tile_mask[1] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -519,8 +591,11 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
   } else if (warp == 1) {
     if (lane == 0) run_mma<D, DIFF>(smem, bars, ctl, tmem, n_kt);
     __syncwarp();
-  } else {
+  } else if (warp < kQk2Warp) {
     run_transform<D, DIFF, NORM, POS, PM>(p, smem, bars, ctl, tmem, bh, qt, n_kt, warp, lane);
+  } else if constexpr (DIFF) {
+    if (lane == 0) run_mma_qk2<D>(smem, bars, ctl, tmem, n_kt);
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -542,6 +617,7 @@ cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
     attr_done = true;
   }
   const unsigned grid = static_cast<unsigned>(p.BH) * static_cast<unsigned>(p.n_qtiles);
+  constexpr int kThreads = threads_for<DIFF>();
   kern<<<grid, kThreads, C::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaErrorLaunchOutOfResources) {
