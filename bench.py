@@ -45,9 +45,12 @@ WORKLOADS = {
     "diff8k_dense": ("diff", 8, 32, 8192, 128, 0.0, 0.5, 2.0, True),
     "rect8k_dense": ("rect", 8, 32, 8192, 128, 0.0, 0.0, 2.0, True),
     # small cases for profiler captures (inputs 168 / 201 MB, above the L2
-    # size; a few hundred microseconds per launch); not bench lines
+    # size; a few hundred microseconds per launch); not bench lines.  The
+    # *_s8k cases keep the full sequence length (CTAs of up to 64 key tiles).
     "diff2k": ("diff", 2, 32, 2048, 128, 1.0, 0.5, 2.0, True),
     "rect2k": ("rect", 4, 32, 2048, 128, 1.0, 0.0, 2.0, True),
+    "diff_s8k": ("diff", 2, 8, 8192, 128, 1.0, 0.5, 2.0, True),
+    "rect_s8k": ("rect", 4, 8, 8192, 128, 1.0, 0.0, 2.0, True),
 }
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}

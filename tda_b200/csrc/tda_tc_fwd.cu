@@ -53,6 +53,14 @@ template <bool DIFF>
 constexpr int threads_for() { return 32 * (2 + kTransformWarps + (DIFF ? 1 : 0)); }
 constexpr int kRkRing = 4;
 constexpr int kHeadGroup = 4;  // (batch, head) slices interleaved in launch order
+// Transform code layout (instruction-cache footprint versus register moves),
+// chosen per form by measurement: the differential transform is twice the
+// code and runs from one rolled chunk loop (the kernel was instruction-fetch
+// bound with both chunks unrolled); the rectified one stays unrolled.
+template <bool DIFF>
+constexpr bool kRollChunks = DIFF;
+template <bool DIFF>
+constexpr bool kRollHalves = false;
 constexpr int kSmemBudget = 232448;  // 227 KB opt-in dynamic shared memory
 
 // status codes (role << 8 | site)
@@ -450,7 +458,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     if (!ok) break;
     tc_fence_after();
     const uint32_t s1col = C::col_s(slot);
-    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS>(
+    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>>(
         tmem + lane_off, s1col, C::kColS2, wg, rk_s + re * C::kRkPerTile, grow - j * kTile, j >= qt, c,
         p.relu_power, p.lam, [&] {
           // S2 is in registers: hand its TMEM slot back so QK2 of the next

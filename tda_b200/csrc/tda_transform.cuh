@@ -96,25 +96,37 @@ __device__ __forceinline__ float2 pow2v(float2 u, float p) {
 // ([16,32)).  P is nonzero only where y = s * rk - tq > 0, so each 16-key half
 // in which no lane of the warp can have a positive y is written as zeros
 // without the power / combine / split work (exact; the common case for the
-// sparse threshold maps TDA produces).  The test:
-//   POS (beta >= 0, tq >= 0) and not on the causal diagonal: first from the
-//     raw scores alone, max_j s_j * max_j rk_j <= tq implies s_j rk_j <= tq
-//     for every j of the half (rkm = per-16-key max of rk; without normalize,
-//     max_j s_j <= tau is already exact); a half this bound cannot clear gets
-//     y formed and tested exactly before any further work;
-//   otherwise: y computed for every entry (diagonal masking, beta < 0).
-// rk1/rk2: this chunk's 32 inverse key norms; rkm1/rkm2: the maxima of its two
-// halves.  Returns this lane's 2-bit mask of halves holding a nonzero P.
-template <int PM, bool DIFF, bool NORM, bool POS, bool MASK>
+// sparse threshold maps TDA produces).
+//   diag: the tile holds the causal diagonal; scores of keys past the row
+//     (index > limit) are replaced by 0 first, as the reference masks them
+//     (triton_threshold_attention.py:79-80).
+//   POS (beta >= 0, tq >= 0): first from the raw scores alone,
+//     max_j s_j * max_j rk_j <= tq implies s_j rk_j <= tq for every j of the
+//     half (rkm = per-16-key max of rk; without normalize max_j s_j <= tau is
+//     already exact); a half this bound cannot clear gets y formed and tested
+//     exactly before any further work.  Masked zeros give y = -tq <= 0.
+//   otherwise (beta < 0): y is formed for every entry.
+// ROLL: the halves run through one rolled loop (the second half is shifted
+// into the first half's registers), which keeps the code small in the
+// instruction cache at the cost of the register moves.  rk1/rk2: this chunk's 32 inverse key norms; rkm1/rkm2:
+// the maxima of its two halves.  Returns this lane's 2-bit mask of halves
+// holding a nonzero P.
+template <int PM, bool DIFF, bool NORM, bool POS, bool ROLL>
 __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t (&b)[32], uint32_t s1_addr,
                                                     const float* rk1, const float* rk2, const float* rkm1,
-                                                    const float* rkm2, int limit, const RowCoef& c, float relu_power,
-                                                    float lam) {
+                                                    const float* rkm2, int limit, bool diag, const RowCoef& c,
+                                                    float relu_power, float lam) {
   constexpr bool kFold = PM != POW_GENERAL;
-  constexpr bool kRaw = POS && !MASK;  // y not precomputed: slow path forms it
-  constexpr bool SAT = NORM && POS;    // normalized scores minus tau <= 1
-  bool lane_nz[2];
-  if constexpr (kRaw) {
+  constexpr bool SAT = NORM && POS;  // normalized scores minus tau <= 1
+  if (diag) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      a[i] = (i <= limit) ? a[i] : 0u;
+      if constexpr (DIFF) b[i] = (i <= limit) ? b[i] : 0u;
+    }
+  }
+  uint32_t lane_nz = 0;  // bit h: this lane may have a positive y in half h
+  if constexpr (POS) {
     float m1[2][2] = {{-3.0e38f, -3.0e38f}, {-3.0e38f, -3.0e38f}};
     float m2[2][2] = {{-3.0e38f, -3.0e38f}, {-3.0e38f, -3.0e38f}};
 #pragma unroll
@@ -141,7 +153,7 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
         const float ms2 = fmaxf(m2[h][0], m2[h][1]);
         nzh = nzh || ((NORM ? ms2 * gm2 : ms2) > c.tq2);
       }
-      lane_nz[h] = nzh;
+      lane_nz |= nzh ? (1u << h) : 0u;
     }
   } else {
     // two independent max chains per 16-key half
@@ -156,42 +168,35 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int i = 4 * e4 + 2 * h;
-        uint32_t x0 = a[i], x1 = a[i + 1];
-        if constexpr (MASK) {
-          x0 = (i <= limit) ? x0 : 0u;
-          x1 = (i + 1 <= limit) ? x1 : 0u;
-        }
         const float2 rr = h ? make_float2(r1.z, r1.w) : make_float2(r1.x, r1.y);
-        const float2 y = NORM ? __ffma2_rn(f2u(x0, x1), rr, make_float2(-c.tq1, -c.tq1))
-                              : __fadd2_rn(f2u(x0, x1), make_float2(-c.tq1, -c.tq1));
+        const float2 y = NORM ? __ffma2_rn(f2u(a[i], a[i + 1]), rr, make_float2(-c.tq1, -c.tq1))
+                              : __fadd2_rn(f2u(a[i], a[i + 1]), make_float2(-c.tq1, -c.tq1));
         a[i] = __float_as_uint(y.x);
         a[i + 1] = __float_as_uint(y.y);
         mx[e4 >> 2][h] = max3f(mx[e4 >> 2][h], y.x, y.y);
         if constexpr (DIFF) {
-          uint32_t w0 = b[i], w1 = b[i + 1];
-          if constexpr (MASK) {
-            w0 = (i <= limit) ? w0 : 0u;
-            w1 = (i + 1 <= limit) ? w1 : 0u;
-          }
           const float2 rs = h ? make_float2(r2.z, r2.w) : make_float2(r2.x, r2.y);
-          const float2 y2 = NORM ? __ffma2_rn(f2u(w0, w1), rs, make_float2(-c.tq2, -c.tq2))
-                                 : __fadd2_rn(f2u(w0, w1), make_float2(-c.tq2, -c.tq2));
+          const float2 y2 = NORM ? __ffma2_rn(f2u(b[i], b[i + 1]), rs, make_float2(-c.tq2, -c.tq2))
+                                 : __fadd2_rn(f2u(b[i], b[i + 1]), make_float2(-c.tq2, -c.tq2));
           b[i] = __float_as_uint(y2.x);
           b[i + 1] = __float_as_uint(y2.y);
           mx[e4 >> 2][h] = max3f(mx[e4 >> 2][h], y2.x, y2.y);
         }
       }
     }
-    lane_nz[0] = fmaxf(mx[0][0], mx[0][1]) > 0.0f;
-    lane_nz[1] = fmaxf(mx[1][0], mx[1][1]) > 0.0f;
+    lane_nz |= fmaxf(mx[0][0], mx[0][1]) > 0.0f ? 1u : 0u;
+    lane_nz |= fmaxf(mx[1][0], mx[1][1]) > 0.0f ? 2u : 0u;
   }
 
   uint32_t nz = 0;
-#pragma unroll
+  constexpr int kUnroll = ROLL ? 1 : 2;
+#pragma unroll kUnroll
   for (int half = 0; half < 2; ++half) {
-    uint32_t hi[8], lo[8];
-    bool any = __any_sync(0xffffffffu, lane_nz[half]);
-    if constexpr (kRaw) {
+    // this half's 16 scores sit in a[o..o+15] (b[o..o+15])
+    const int o = ROLL ? 0 : 16 * half;
+    bool lnz = (lane_nz >> half) & 1u;
+    bool any = __any_sync(0xffffffffu, lnz);
+    if constexpr (POS) {
       if (any) {
         // the bound could not clear this half: form y exactly and test again
         float mx[2] = {-3.0e38f, -3.0e38f};
@@ -204,7 +209,7 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
           }
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            const int i = 16 * half + 4 * q4 + 2 * t;
+            const int i = o + 4 * q4 + 2 * t;
             const float2 rr = t ? make_float2(r1.z, r1.w) : make_float2(r1.x, r1.y);
             const float2 y = NORM ? __ffma2_rn(f2u(a[i], a[i + 1]), rr, make_float2(-c.tq1, -c.tq1))
                                   : __fadd2_rn(f2u(a[i], a[i + 1]), make_float2(-c.tq1, -c.tq1));
@@ -221,20 +226,20 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
             }
           }
         }
-        lane_nz[half] = fmaxf(mx[0], mx[1]) > 0.0f;
-        any = __any_sync(0xffffffffu, lane_nz[half]);
+        lnz = fmaxf(mx[0], mx[1]) > 0.0f;
+        any = __any_sync(0xffffffffu, lnz);
       }
     }
-    nz |= lane_nz[half] ? (1u << half) : 0u;
+    nz |= lnz ? (1u << half) : 0u;
+    uint32_t hi[8], lo[8];
     if (any) {
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        const int e2 = 8 * half + q;
-        const float2 y1 = f2u(a[2 * e2], a[2 * e2 + 1]);
+        const float2 y1 = f2u(a[o + 2 * q], a[o + 2 * q + 1]);
         const float2 u1 = NORM ? scaled_relu<SAT>(y1, c.rq1) : relu2(y1);
         float2 P;
         if constexpr (DIFF) {
-          const float2 y2 = f2u(b[2 * e2], b[2 * e2 + 1]);
+          const float2 y2 = f2u(b[o + 2 * q], b[o + 2 * q + 1]);
           const float2 u2 = (NORM || kFold) ? scaled_relu<SAT>(y2, c.rq2) : relu2(y2);
           if constexpr (kFold) {
             P = sub2(pow2v<PM>(u1, relu_power), pow2v<PM>(u2, relu_power));
@@ -260,6 +265,13 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
     }
     tmem_st8(s1_addr + 8 * half, hi);
     tmem_st8(s1_addr + 16 + 8 * half, lo);
+    if (ROLL && half == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        a[i] = a[16 + i];
+        if constexpr (DIFF) b[i] = b[16 + i];
+      }
+    }
   }
   return nz;
 }
@@ -272,61 +284,61 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
 // called as soon as it sits in registers, so the next tile's QK2 can reuse the
 // S2 columns while this tile is transformed; S1 of the second chunk is loaded
 // after the first chunk is done (keeps register use down).  The rectified
-// form loads both of its S chunks at once.
+// form loads both of its S chunks at once.  ROLL_C: the chunks run through one
+// rolled loop (the second chunk's registers are moved into the first's);
+// ROLL_H: likewise for the two halves of a chunk.
 // Returns bit (2 cc + h): 16-key half h of chunk cc holds a nonzero P.
-template <int PM, bool DIFF, bool NORM, bool POS, typename ReleaseS2>
+template <int PM, bool DIFF, bool NORM, bool POS, bool ROLL_C, bool ROLL_H, typename ReleaseS2>
 __device__ __forceinline__ uint32_t transform_tile(uint32_t tmem_row, uint32_t s1col, uint32_t s2col, int wg,
                                                    const float* rk_tile, int limit0, bool diag, const RowCoef& c,
                                                    float relu_power, float lam, ReleaseS2&& release_s2) {
+  constexpr int kMaxOff = DIFF ? 256 : 128;  // rkmax after rk1 (and rk2)
   const int ch0 = 2 * wg;
   uint32_t nz = 0;
+  uint32_t a[32], b[32], b1[32];
   if constexpr (DIFF) {
-    uint32_t a[32];
-    uint32_t b[2][32];
     tmem_ld32(tmem_row + s1col + 32 * ch0, a);
-    tmem_ld32(tmem_row + s2col + 32 * ch0, b[0]);
-    tmem_ld32(tmem_row + s2col + 32 * (ch0 + 1), b[1]);
+    tmem_ld32(tmem_row + s2col + 32 * ch0, b);
+    tmem_ld32(tmem_row + s2col + 32 * (ch0 + 1), b1);
     tmem_wait_ld();
     release_s2();
-#pragma unroll
+  } else {
+    tmem_ld32(tmem_row + s1col + 32 * ch0, a);
+    tmem_ld32(tmem_row + s1col + 32 * (ch0 + 1), b1);
+    tmem_wait_ld();
+  }
+  auto chunk = [&](uint32_t(&x)[32], uint32_t(&y)[32], int cc) {
+    const int ch = ch0 + cc;
+    const float* r1 = rk_tile + 32 * ch;
+    const float* m1 = rk_tile + kMaxOff + 2 * ch;
+    nz |= transform_chunk<PM, DIFF, NORM, POS, ROLL_H>(x, y, tmem_row + s1col + 32 * ch, r1, r1 + 128, m1, m1 + 8,
+                                                       limit0 - 32 * ch, diag, c, relu_power, lam)
+          << (2 * cc);
+  };
+  if constexpr (ROLL_C) {
+#pragma unroll 1
     for (int cc = 0; cc < 2; ++cc) {
-      const int ch = ch0 + cc;
       if (cc == 1) {
-        tmem_ld32(tmem_row + s1col + 32 * ch, a);
-        tmem_wait_ld();
+        if constexpr (DIFF) {
+          tmem_ld32(tmem_row + s1col + 32 * (ch0 + 1), a);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) b[i] = b1[i];
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a[i] = b1[i];
+        }
       }
-      const uint32_t s1 = tmem_row + s1col + 32 * ch;
-      const float* r1 = rk_tile + 32 * ch;
-      const float* m1 = rk_tile + 256 + 2 * ch;
-      const int limit = limit0 - 32 * ch;
-      if (diag)
-        nz |= transform_chunk<PM, DIFF, NORM, POS, true>(a, b[cc], s1, r1, r1 + 128, m1, m1 + 8, limit, c,
-                                                         relu_power, lam)
-              << (2 * cc);
-      else
-        nz |= transform_chunk<PM, DIFF, NORM, POS, false>(a, b[cc], s1, r1, r1 + 128, m1, m1 + 8, limit, c,
-                                                          relu_power, lam)
-              << (2 * cc);
+      chunk(a, b, cc);
     }
   } else {
-    uint32_t a[2][32];
-    tmem_ld32(tmem_row + s1col + 32 * ch0, a[0]);
-    tmem_ld32(tmem_row + s1col + 32 * (ch0 + 1), a[1]);
-    tmem_wait_ld();
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      const int ch = ch0 + cc;
-      const uint32_t s1 = tmem_row + s1col + 32 * ch;
-      const float* r1 = rk_tile + 32 * ch;
-      const float* m1 = rk_tile + 128 + 2 * ch;
-      const int limit = limit0 - 32 * ch;
-      if (diag)
-        nz |= transform_chunk<PM, DIFF, NORM, POS, true>(a[cc], a[cc], s1, r1, r1, m1, m1, limit, c, relu_power, lam)
-              << (2 * cc);
-      else
-        nz |= transform_chunk<PM, DIFF, NORM, POS, false>(a[cc], a[cc], s1, r1, r1, m1, m1, limit, c, relu_power,
-                                                          lam)
-              << (2 * cc);
+    chunk(a, b, 0);
+    if constexpr (DIFF) {
+      tmem_ld32(tmem_row + s1col + 32 * (ch0 + 1), a);
+      tmem_wait_ld();
+      chunk(a, b1, 1);
+    } else {
+      chunk(b1, b, 1);
     }
   }
   return nz;
