@@ -332,13 +332,45 @@ def run_tda(args, rank, local, world):
     d2h = host_out.numel() * host_out.element_size()
     betat, lamt = torch.tensor(beta), torch.tensor(lam)
 
+    # (batch, head) slices are independent, so the step streams chunks of
+    # heads: host->device copy of chunk c+1 (copy engine), the public API on
+    # chunk c (compute stream) and device->host copy of chunk c-1 (second copy
+    # engine) overlap.  Every byte of every input and of the output crosses
+    # PCIe inside the timed region.
+    dev_in = [torch.empty_like(x) for x in xs]
+    n_chunks = min(n_bh, 8)
+    bounds = [(c * n_bh // n_chunks, (c + 1) * n_bh // n_chunks) for c in range(n_chunks)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
     def e2e_step():
-        d = [h.to(dev, non_blocking=True) for h in host_in]
-        if op == "diff":
-            o = tda_b200.differential_threshold_rela_triton(*d, betat, lamt, p, norm)
-        else:
-            o = tda_b200.threshold_rela_triton(*d, betat, p, norm)
-        host_out.copy_(o, non_blocking=True)
+        start = torch.cuda.Event()
+        start.record(stream)
+        s_in.wait_event(start)
+        s_out.wait_event(start)
+        ready = []
+        with torch.cuda.stream(s_in):
+            for a, b in bounds:
+                for hbuf, dbuf in zip(host_in, dev_in):
+                    dbuf[:, a:b].copy_(hbuf[:, a:b], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_in)
+                ready.append(e)
+        for (a, b), e in zip(bounds, ready):
+            stream.wait_event(e)
+            d = [x[:, a:b] for x in dev_in]
+            if op == "diff":
+                o = tda_b200.differential_threshold_rela_triton(*d, betat, lamt, p, norm)
+            else:
+                o = tda_b200.threshold_rela_triton(*d, betat, p, norm)
+            done = torch.cuda.Event()
+            done.record(stream)
+            s_out.wait_event(done)
+            o.record_stream(s_out)
+            with torch.cuda.stream(s_out):
+                host_out[:, a:b].copy_(o, non_blocking=True)
+        end = torch.cuda.Event()
+        end.record(s_out)
+        stream.wait_event(end)
 
     e2e_steps = max(1, min(args.steps, 5))
     e2e_step()
@@ -399,7 +431,10 @@ def run_tda(args, rank, local, world):
                 "peak_source": f"bf16_tflops (burst) of {peak_src}",
             },
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
+            "e2e": {"value": e2e_val, "unit": "TFLOP/s",
+                    "how": f"public API on {n_chunks} chunks of (batch, head) slices per rank; pinned-host "
+                           "inputs in and output out, copies overlapped with compute on two copy streams",
+                    "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
