@@ -1,4 +1,4 @@
-"""CPU restatement of the TDA forward pass -- TEST INFRASTRUCTURE ONLY.
+"""CPU restatement of the TDA forward and backward passes -- TEST INFRASTRUCTURE ONLY.
 
 This module is the checker for the CUDA path, never the thing measured or
 shipped.  Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg
@@ -19,6 +19,10 @@ It restates, in numpy, the arithmetic of the reference ``triton_threshold_attent
 * ``differential_threshold_rela_triton``  (triton_threshold_attention.py:489-519)
     - optional F.normalize(p=2, dim=-1, eps=1e-12) of q1, k1, q2, k2 (:505-509)
     - out = rect(q1, k1, v) - clamp(lambda, 0, 1) * rect(q2, k2, v) (:512-517)
+* the backward kernels ``_threshold_rela_bwd_kernel_dq`` / ``_dkv``
+  (triton_threshold_attention.py:118-324) and ``ThresholdRelaFunction.backward``
+  (:405-469), plus the gradients torch autograd adds around them in the
+  differential form (F.normalize, clamp(lambda), the combine)
 * ``threshold_rela_triton``  (triton_threshold_attention.py:472-486) has no
   ``normalize`` argument in the reference; ``normalize=True`` here means the
   reference called on F.normalize(q), F.normalize(k), exactly as each branch of
@@ -127,6 +131,113 @@ def diff_fwd(q1, q2, k1, k2, v, beta, lambda_param, relu_power_: float = 2.0,
     return o1 - dtype(lam) * o2
 
 
+def relu_power_grad(z: np.ndarray, p: float) -> np.ndarray:
+    """d relu(z)^p / dz as the reference's backward kernels form it
+    (triton_threshold_attention.py:195-206 and :294-304): 2 relu(z) for p == 2,
+    1{z > 0} for p == 1, else p * exp((p - 1) * log(relu(z) + 1e-10)) where
+    relu(z) > 0."""
+    x = np.maximum(z, z.dtype.type(0))
+    if p == 2.0:
+        return z.dtype.type(2) * x
+    if p == 1.0:
+        return np.where(z > 0, z.dtype.type(1), z.dtype.type(0))
+    with np.errstate(divide="ignore"):
+        y = z.dtype.type(p) * np.exp(z.dtype.type(p - 1.0) * np.log(x + z.dtype.type(POW_EPS)))
+    return np.where(x > 0, y, z.dtype.type(0))
+
+
+def rect_bwd_core(q, k, v, dout, beta, relu_power_: float = 2.0, dtype=np.float64,
+                  row_chunk: int = 512):
+    """Gradients of the rectified forward w.r.t. its (already normalized) q, k
+    and v, formed as the reference's two backward kernels form them
+    (triton_threshold_attention.py:118-224 for dQ, :227-324 for dK / dV):
+
+      s_ij  = q_i . k_j, set to 0 for j > i          (recomputed, :186-190, :282-286)
+      z_ij  = s_ij - tau_i
+      dP_ij = dout_i . v_j                             (:211, :312)
+      dA_ij = dP_ij * relu_power_grad(z_ij)            (:214, :313)
+      dq_i  = sum_j dA_ij k_j     over every key j     (:219)
+      dk_j  = sum_i dA_ij q_i     over every query i   (:317)
+      dv_j  = sum_i relu(z_ij)^p dout_i                (:307)
+
+    The mask zeroes s_ij but dA_ij is not masked, so with beta < 0 (tau < 0,
+    z_ij = -tau_i > 0 on masked entries) the reference's dq and dk take
+    contributions from keys after the query row; they are kept here.  With
+    beta >= 0 those entries have zero gradient.  Returns (dq, dk, dv) shaped
+    like q, in ``dtype``.
+    """
+    q, k, v, dout = _as_bhsd(q), _as_bhsd(k), _as_bhsd(v), _as_bhsd(dout)
+    B, H, S, D = q.shape
+    p = float(relu_power_)
+    tau = tau_vector(S, D, float(beta)).astype(dtype)
+    qf, kf, vf, gf = (x.reshape(B * H, S, D).astype(dtype) for x in (q, k, v, dout))
+    dq = np.zeros((B * H, S, D), dtype=dtype)
+    dk = np.zeros_like(dq)
+    dv = np.zeros_like(dq)
+    zero = dtype(0)
+    keys = np.arange(S)
+    for b in range(B * H):
+        for c0 in range(0, S, row_chunk):
+            r = np.arange(c0, min(S, c0 + row_chunk))
+            s = qf[b, r] @ kf[b].T
+            s = np.where(keys[None, :] <= r[:, None], s, zero)
+            z = s - tau[r][:, None]
+            x = np.maximum(z, zero)
+            P = relu_power(x, p)
+            dA = (gf[b, r] @ vf[b].T) * relu_power_grad(z, p)
+            dq[b, r] = dA @ kf[b]
+            dk[b] += dA.T @ qf[b, r]
+            dv[b] += P.T @ gf[b, r]
+    return tuple(x.reshape(B, H, S, D) for x in (dq, dk, dv))
+
+
+def l2_normalize_bwd(x, g, dtype=np.float64) -> np.ndarray:
+    """Gradient through y = x / max(||x||, eps) (torch F.normalize): for
+    ||x|| > eps, (g - y (y . g)) / ||x||; otherwise g / eps."""
+    x = np.asarray(x, dtype=dtype)
+    g = np.asarray(g, dtype=dtype)
+    n = np.sqrt(np.sum(x * x, axis=-1, keepdims=True))
+    big = n > dtype(NORM_EPS)
+    nn = np.where(big, n, dtype(1))
+    y = x / nn
+    gx = (g - y * np.sum(y * g, axis=-1, keepdims=True)) / nn
+    return np.where(big, gx, g / dtype(NORM_EPS))
+
+
+def rect_bwd(q, k, v, dout, beta, relu_power_: float = 2.0, normalize: bool = False,
+             dtype=np.float64):
+    """Gradients of ``rect_fwd(q, k, v, beta, p, normalize)`` w.r.t. q, k, v:
+    the reference's backward kernels on F.normalize'd q, k when ``normalize``,
+    chained through F.normalize (as torch autograd does around the reference
+    op, triton_threshold_attention.py:505-512)."""
+    qn = l2_normalize(q, dtype) if normalize else np.asarray(q, dtype=dtype)
+    kn = l2_normalize(k, dtype) if normalize else np.asarray(k, dtype=dtype)
+    dq, dk, dv = rect_bwd_core(qn, kn, v, dout, beta, relu_power_, dtype)
+    if normalize:
+        dq = l2_normalize_bwd(q, dq, dtype)
+        dk = l2_normalize_bwd(k, dk, dtype)
+    return dq, dk, dv
+
+
+def diff_bwd(q1, q2, k1, k2, v, dout, beta, lambda_param, relu_power_: float = 2.0,
+             normalize: bool = True, dtype=np.float64):
+    """Gradients of ``diff_fwd`` (triton_threshold_attention.py:489-519) w.r.t.
+    q1, q2, k1, k2, v and lambda: branch 1 with dout, branch 2 with
+    -clamp(lambda) * dout, dv summed, and d lambda = -sum(out2 * dout) where
+    torch.clamp passes the gradient (0 <= lambda <= 1), else 0."""
+    lam = float(lambda_param)
+    lamc = min(max(lam, 0.0), 1.0)
+    dout = np.asarray(dout, dtype=dtype)
+    dq1, dk1, dv1 = rect_bwd(q1, k1, v, dout, beta, relu_power_, normalize, dtype)
+    dq2, dk2, dv2 = rect_bwd(q2, k2, v, -dtype(lamc) * dout, beta, relu_power_, normalize, dtype)
+    if 0.0 <= lam <= 1.0:
+        o2 = rect_fwd(q2, k2, v, beta, relu_power_, normalize, dtype)
+        dlam = -float(np.sum(o2 * dout))
+    else:
+        dlam = 0.0
+    return dq1, dq2, dk1, dk2, dv1 + dv2, dlam
+
+
 def rel_l2(a, b) -> float:
     """||a - b||_2 / ||b||_2 over all entries, in float64 (NaN entries of b, i.e.
     rows outside a sample, are skipped)."""
@@ -150,6 +261,14 @@ def bf16_round(x) -> np.ndarray:
     u = ((u + rounding) >> 16) << 16
     out = (u & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
     return np.where(nan, np.float32(np.nan), out)
+
+
+def bwd_flops(batch_heads: int, seq_len: int, head_dim: int, differential: bool) -> float:
+    """Dense causal algorithmic FLOPs of the backward: per branch five GEMMs of
+    2*S*S*D/2 per (batch, head) -- recomputed S, dP = dout V^T, dV = P^T dout,
+    dQ = dA K, dK = dA^T Q -- twice for the differential form."""
+    gemms = 10 if differential else 5
+    return float(gemms) * float(batch_heads) * float(seq_len) ** 2 * float(head_dim)
 
 
 def flops(batch_heads: int, seq_len: int, head_dim: int, differential: bool) -> float:
