@@ -90,6 +90,25 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                  float lambda_param, float relu_power, int normalize, void* workspace, size_t workspace_bytes,
                  int* status, void* stream);
 
+/* Backward of one threshold rectified attention branch, given the upstream
+ * gradient dout of its output (same shape and dtype as q):
+ *   dq, dk, dv = gradients w.r.t. q, k, v of rect(q, k, v) for the gradient
+ *   dout_scale * dout, in fp32 (batch_heads, seq_len, head_dim) arrays.
+ * Replaces ThresholdRelaFunction.backward (triton_threshold_attention.py:405-469)
+ * and its kernels _threshold_rela_bwd_kernel_dq (:118-224) and
+ * _threshold_rela_bwd_kernel_dkv (:227-324), including their handling of
+ * masked entries: dQ / dK are not masked, so with beta < 0 keys after a query
+ * row contribute as they do in the reference.  normalize != 0: q, k are
+ * F.normalize'd inside and dq, dk are chained back through F.normalize (torch
+ * autograd's part of :505-512).  accumulate_dv != 0 adds into dv (the
+ * differential form calls this once per branch: dout_scale = 1, then
+ * -clamp(lambda, 0, 1) with accumulate_dv = 1).  dtype: TDA_F32 or TDA_BF16
+ * inputs; head_dim 16, 32, 64 or 128; exact fp32 arithmetic on CUDA cores.
+ * dq, dk, dv must not alias the inputs. */
+int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, int dtype, float* dq, float* dk,
+                 float* dv, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,
+                 int normalize, float dout_scale, int accumulate_dv, void* stream);
+
 /* Stage 1 of the normalized tensor-core path, exposed so callers can time or
  * reuse it.  Writes the key table of k into rk (batch_heads * pad * 17 / 16
  * floats, pad = seq_len rounded up to 128): rk[bh * pad + j] =

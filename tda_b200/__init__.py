@@ -1,4 +1,4 @@
-"""tda_b200: B200-native (sm_100a) Threshold (Differential) Attention forward.
+"""tda_b200: B200-native (sm_100a) Threshold (Differential) Attention (forward and backward).
 
 Drop-in for the public API of snap-research/TDA's ``triton_threshold_attention``
 module; see ``tda_b200.triton_threshold_attention`` for the same module name.
@@ -9,6 +9,7 @@ from .ops import (  # noqa: F401
     check_status,
     diff_forward,
     differential_threshold_rela_triton,
+    rect_backward,
     rect_forward,
     threshold_rela_triton,
 )
@@ -19,6 +20,7 @@ __all__ = [
     "ThresholdRelaFunction",
     "DifferentialThresholdRelaFunction",
     "rect_forward",
+    "rect_backward",
     "diff_forward",
     "check_status",
 ]

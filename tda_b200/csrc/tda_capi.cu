@@ -263,4 +263,41 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                          relu_power, normalize, rk1, rk2, status, stream);
 }
 
+int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, int dtype, float* dq, float* dk,
+                 float* dv, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,
+                 int normalize, float dout_scale, int accumulate_dv, void* stream) {
+  if (batch_heads < 1 || seq_len < 1)
+    return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1 (got %lld, %lld)",
+                static_cast<long long>(batch_heads), static_cast<long long>(seq_len));
+  if (dtype != TDA_F32 && dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
+  if (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128)
+    return fail(TDA_ERR_UNSUPPORTED, "backward supports head_dim 16, 32, 64 or 128 (got %lld)",
+                static_cast<long long>(head_dim));
+  if (seq_len > (1ll << 30)) return fail(TDA_ERR_INVALID, "seq_len too large (%lld)", static_cast<long long>(seq_len));
+  if (batch_heads * ((seq_len + 63) / 64) > 0x7fffffffll)
+    return fail(TDA_ERR_INVALID, "batch_heads * seq_len tiles exceed the grid limit");
+  const void* ptrs[7] = {q, k, v, dout, dq, dk, dv};
+  for (const void* ptr : ptrs)
+    if (!ptr || !aligned16(ptr)) return fail(TDA_ERR_INVALID, "q, k, v, dout, dq, dk, dv must be 16-byte aligned");
+  tda::BwdParams prm{};
+  prm.q = q;
+  prm.k = k;
+  prm.v = v;
+  prm.dout = dout;
+  prm.dq = dq;
+  prm.dk = dk;
+  prm.dv = dv;
+  prm.S = static_cast<int>(seq_len);
+  prm.BH = static_cast<int>(batch_heads);
+  prm.beta = beta;
+  prm.relu_power = relu_power;
+  prm.dout_scale = dout_scale;
+  prm.normalize = normalize ? 1 : 0;
+  prm.accumulate_dv = accumulate_dv ? 1 : 0;
+  cudaError_t ce = tda::launch_rect_bwd(prm, static_cast<int>(head_dim), dtype == TDA_BF16,
+                                        static_cast<cudaStream_t>(stream));
+  if (ce != cudaSuccess) return cuda_fail(ce, "backward kernel launch");
+  return TDA_OK;
+}
+
 }  // extern "C"

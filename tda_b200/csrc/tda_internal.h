@@ -75,6 +75,27 @@ struct SimtFwdParams {
 
 cudaError_t launch_simt_fwd(const SimtFwdParams& p, int head_dim, cudaStream_t stream);
 
+// CUDA-core fp32 backward of one rectified branch (dq, dk through F.normalize
+// when normalize; dv written or accumulated).  Inputs bf16 or fp32.
+struct BwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* dout;
+  float* dq;
+  float* dk;
+  float* dv;
+  int S;
+  int BH;
+  float beta;
+  float relu_power;
+  float dout_scale;
+  int normalize;
+  int accumulate_dv;
+};
+
+cudaError_t launch_rect_bwd(const BwdParams& p, int head_dim, bool in_bf16, cudaStream_t stream);
+
 // Key table of x: rk[bh][j] = 1 / max(||x[bh][j]||_2, 1e-12) for j < S, 0 for
 // S <= j < S_pad, followed by rkmax[bh][g] = max of rk over keys [16 g, 16 g + 16).
 inline size_t key_table_floats(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * padded_seq(S) / 16 * 17; }

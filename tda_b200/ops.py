@@ -12,8 +12,9 @@ behaviour:
   relu_power=2.0, normalize=True)`` -- reference :489-519, computed in ONE
   fused pass over the keys (one launch instead of two forward kernels plus
   the torch normalize / clamp / combine ops).
-* ``ThresholdRelaFunction`` -- reference :327-469 (forward only here; its
-  backward raises NotImplementedError).
+* ``ThresholdRelaFunction`` -- reference :327-469, forward and backward
+  (``rect_backward``: the reference's dQ / dK / dV kernels, :118-324, on CUDA
+  cores in fp32, head_dim 16-128).
 
 Data path: CUDA tensors only.  bf16 with head_dim 64/128 runs the tcgen05
 tensor-core kernel; fp32 runs the exact-fp32 CUDA-core kernel; other dtypes /
@@ -162,32 +163,108 @@ def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normaliz
     return _finish(out, orig, out_dtype)
 
 
+def rect_backward(q, k, v, dout, beta, relu_power=2.0, normalize: bool = False, dout_scale: float = 1.0,
+                  dv: torch.Tensor | None = None):
+    """Gradients (dq, dk, dv), fp32, of ``rect_forward(q, k, v, beta, p,
+    normalize)`` for the upstream gradient ``dout_scale * dout``, as the
+    reference's backward computes them (:405-469, kernels :118-324; masked
+    entries included in dQ / dK, which matters for beta < 0).  When ``dv`` (an
+    fp32 tensor of v's shape) is given, the value gradient is added into it."""
+    assert q.shape == k.shape == v.shape == dout.shape
+    beta_v = _scalar(beta)
+    p_v = _scalar(relu_power)
+    for t in (q, k, v, dout):
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise RuntimeError("threshold attention backward: tda_b200 runs on CUDA tensors only; "
+                               "there is no CPU fallback")
+    B, H, S, D = q.shape
+    all_bf16 = all(t.dtype == torch.bfloat16 for t in (q, k, v, dout))
+    kind, cdt = (_lib.TDA_BF16, torch.bfloat16) if all_bf16 else (_lib.TDA_F32, torch.float32)
+    qc, kc, vc, gc = (t.to(cdt).contiguous() for t in (q, k, v, dout))
+    dq = torch.empty((B, H, S, D), dtype=torch.float32, device=qc.device)
+    dk = torch.empty_like(dq)
+    accumulate = dv is not None
+    if dv is None:
+        dv = torch.empty_like(dq)
+    elif dv.dtype != torch.float32 or not dv.is_contiguous() or dv.shape != dq.shape:
+        raise ValueError("dv must be a contiguous fp32 tensor of v's shape")
+    if dq.numel() == 0:
+        return dq, dk, dv
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(qc.device).cuda_stream
+    with torch.cuda.device(qc.device):
+        rc = lib.tda_rect_bwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gc.data_ptr(), kind, dq.data_ptr(),
+                              dk.data_ptr(), dv.data_ptr(), B * H, S, D, beta_v, p_v, int(normalize),
+                              float(dout_scale), int(accumulate), stream)
+    _lib.check(rc)
+    return dq, dk, dv
+
+
 class ThresholdRelaFunction(torch.autograd.Function):
     """Threshold Rectified Attention (reference :327-469).
 
-    forward(q, k, v, beta, relu_power[, normalize]) -> out.  The backward pass
-    is not implemented yet and raises NotImplementedError instead of
-    returning wrong or missing gradients."""
+    forward(q, k, v, beta, relu_power[, normalize]) -> out; backward returns
+    dq, dk, dv in the inputs' dtypes (beta and relu_power get no gradient, as
+    in the reference, :469)."""
 
     @staticmethod
     def forward(ctx, q, k, v, beta, relu_power, normalize=False):
-        return rect_forward(q, k, v, beta, relu_power, normalize)
+        out = rect_forward(q, k, v, beta, relu_power, normalize)
+        ctx.save_for_backward(q, k, v)
+        ctx.beta = _scalar(beta)
+        ctx.relu_power = _scalar(relu_power)
+        ctx.normalize = bool(normalize)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
-        raise NotImplementedError("tda_b200: the backward pass of threshold attention is not implemented")
+        q, k, v = ctx.saved_tensors
+        dq, dk, dv = rect_backward(q, k, v, dout, ctx.beta, ctx.relu_power, ctx.normalize)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
 
 
 class DifferentialThresholdRelaFunction(torch.autograd.Function):
-    """Fused threshold differential attention; forward only (backward raises)."""
+    """Fused threshold differential attention.  Backward: each branch through
+    the branch backward (branch 2 with -clamp(lambda) * dout, dv summed), and
+    d lambda = -sum(out2 * dout) where torch.clamp passes the gradient
+    (0 <= lambda <= 1), as torch autograd gives it around the reference
+    (:512-517)."""
 
     @staticmethod
     def forward(ctx, q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize):
-        return diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize)
+        out = diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize)
+        lam_t = lambda_param if isinstance(lambda_param, torch.Tensor) else None
+        ctx.save_for_backward(q1, q2, k1, k2, v, lam_t)
+        ctx.lam_float = None if lam_t is not None else float(lambda_param)
+        ctx.beta = _scalar(beta)
+        ctx.relu_power = _scalar(relu_power)
+        ctx.normalize = bool(normalize)
+        return out
 
     @staticmethod
     def backward(ctx, dout):
-        raise NotImplementedError("tda_b200: the backward pass of threshold attention is not implemented")
+        q1, q2, k1, k2, v, lam_t = ctx.saved_tensors
+        beta, p, norm = ctx.beta, ctx.relu_power, ctx.normalize
+        dq1, dk1, dv = rect_backward(q1, k1, v, dout, beta, p, norm)
+        if lam_t is None or lam_t.numel() == 1:
+            lam = ctx.lam_float if lam_t is None else _scalar(lam_t)
+            lamc = min(max(lam, 0.0), 1.0)
+            dq2, dk2, dv = rect_backward(q2, k2, v, dout, beta, p, norm, dout_scale=-lamc, dv=dv)
+        else:
+            # broadcastable lambda: the second branch sees -clamp(lambda) * dout
+            lamc = torch.clamp(lam_t.to(device=dout.device, dtype=torch.float32), min=0.0, max=1.0)
+            d2 = (-lamc * dout.float()).contiguous()
+            dq2, dk2, dv = rect_backward(q2, k2, v, d2, beta, p, norm, dv=dv)
+        dlam = None
+        if lam_t is not None and ctx.needs_input_grad[6]:
+            o2 = rect_forward(q2, k2, v, beta, p, norm, out_dtype=torch.float32)
+            g = -(o2 * dout.float())
+            lam32 = lam_t.to(device=dout.device, dtype=torch.float32)
+            inside = ((lam32 >= 0.0) & (lam32 <= 1.0)).to(torch.float32)
+            dlam = (g.sum() * inside if lam_t.numel() == 1 else g.sum_to_size(lam_t.shape) * inside)
+            dlam = dlam.reshape(lam_t.shape).to(device=lam_t.device, dtype=lam_t.dtype)
+        return (dq1.to(q1.dtype), dq2.to(q2.dtype), dk1.to(k1.dtype), dk2.to(k2.dtype), dv.to(v.dtype), None, dlam,
+                None, None)
 
 
 def threshold_rela_triton(q, k, v, beta, relu_power=2.0, normalize=False):

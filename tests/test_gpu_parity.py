@@ -239,8 +239,13 @@ def test_errors_and_autograd():
     qg = q.clone().requires_grad_(True)
     out = tda_b200.threshold_rela_triton(qg, q, q, torch.tensor(1.0), 2.0)
     assert out.requires_grad
-    with pytest.raises(NotImplementedError):
-        out.float().sum().backward()
+    out.float().sum().backward()
+    assert qg.grad is not None and qg.grad.shape == q.shape and qg.grad.dtype == q.dtype
+    # head_dim 256 runs forward; its backward is not built and says so
+    x = torch.randn(1, 1, 32, 256, device=DEV, requires_grad=True)
+    y = tda_b200.threshold_rela_triton(x, x.detach(), x.detach(), 1.0)
+    with pytest.raises(ValueError, match="head_dim"):
+        y.sum().backward()
     empty = torch.zeros(1, 2, 0, 64, device=DEV, dtype=torch.bfloat16)
     assert tda_b200.threshold_rela_triton(empty, empty, empty, 1.0).shape == empty.shape
 
