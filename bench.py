@@ -224,6 +224,102 @@ def run_reference(args, rank, world):
     return 0
 
 
+# ------------------------------------------------------------------- backward
+def run_tda_backward(args, rank, local, world):
+    """--backward: the backward pass (tda_rect_bwd per branch) of the workload,
+    device-resident inputs and upstream gradient; value = algorithmic backward
+    TFLOP/s (five GEMMs of 2*S*S*D/2 per branch and (batch, head))."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from oracle.tda_oracle import bwd_flops
+    from tda_b200 import _lib
+    from tda_b200.shard import max_over_ranks, shard_range
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    name = args.config
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    shard = shard_range(B * H, world, rank)
+    xs = make_inputs(name, shard, dev)
+    g = torch.Generator(device=dev).manual_seed(777 + shard.start)
+    dout = torch.randn(xs[0].shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    n_bh = shard.size
+    lib = _lib.load()
+    grads = [torch.empty(xs[0].shape, dtype=torch.float32, device=dev) for _ in range(5)]
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    ptr = [x.data_ptr() for x in xs]
+    lamc = min(max(lam, 0.0), 1.0)
+
+    def step():
+        if op == "diff":
+            _lib.check(lib.tda_rect_bwd(ptr[0], ptr[2], ptr[4], dout.data_ptr(), _lib.TDA_BF16, grads[0].data_ptr(),
+                                        grads[2].data_ptr(), grads[4].data_ptr(), n_bh, S, D, beta, p, int(norm),
+                                        1.0, 0, sp))
+            _lib.check(lib.tda_rect_bwd(ptr[1], ptr[3], ptr[4], dout.data_ptr(), _lib.TDA_BF16, grads[1].data_ptr(),
+                                        grads[3].data_ptr(), grads[4].data_ptr(), n_bh, S, D, beta, p, int(norm),
+                                        -lamc, 1, sp))
+        else:
+            _lib.check(lib.tda_rect_bwd(ptr[0], ptr[1], ptr[2], dout.data_ptr(), _lib.TDA_BF16, grads[0].data_ptr(),
+                                        grads[1].data_ptr(), grads[2].data_ptr(), n_bh, S, D, beta, p, int(norm),
+                                        1.0, 0, sp))
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    clocks = ClockSampler(gpu_smi_id(local)) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ms = max_over_ranks(e0.elapsed_time(e1), dev)
+    fl = bwd_flops(B * H, S, D, op == "diff")
+    value = fl * args.steps / (ms / 1e3) / 1e12
+    peaks, peak_src = load_peaks()
+    sm_mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12  # nominal FFMA rate of the CUDA cores
+    achieved = bwd_flops(n_bh, S, D, op == "diff") * args.steps / (e0.elapsed_time(e1) / 1e3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": f"TDA backward TFLOP/s ({name})", "value": value, "unit": "TFLOP/s", "impl": "tda",
+            "pass": "backward", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 arithmetic on bf16 inputs", "data": "synthetic",
+            "config": {"workload": describe(name) + " backward", "batch": B, "heads": H, "seq_len": S,
+                       "head_dim": D, "flops_per_step": fl,
+                       "executed_flops_per_step": fl * 7.0 / 5.0,
+                       "kernels": "tda_bwd_dq_kernel + tda_bwd_dkv_kernel per branch (CUDA-core fp32)"},
+            "roofline": {"bound": "fp32 CUDA cores", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
+                         "frac": achieved / fp32_peak, "traffic": None,
+                         "peak_source": "nominal: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz "
+                                        f"({sm_mhz:.0f} MHz, {peak_src} peaks file)"},
+            "cpu_baseline": None, "e2e": None,
+            "gpu_launches": (4 if op == "diff" else 2) * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 # ------------------------------------------------------------------- GPU arm
 def make_inputs(name, shard, device):
     """Seeded N(0,1) inputs per (tensor, flattened head): identical data for a
@@ -455,12 +551,16 @@ def main():
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="diff8k")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--backward", action="store_true",
+                    help="time the backward pass of the workload instead of the forward")
     ap.add_argument("--ref-rows", type=int, default=256, help="query rows per reference-arm step")
     args = ap.parse_args()
     from tda_b200.shard import env_rank_world
     rank, local, world = env_rank_world()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.backward:
+        return run_tda_backward(args, rank, local, world)
     return run_tda(args, rank, local, world)
 
 
