@@ -260,19 +260,22 @@ def run_tda_backward(args, rank, local, world):
     sp = stream.cuda_stream
     ptr = [x.data_ptr() for x in xs]
     lamc = min(max(lam, 0.0), 1.0)
+    ws_n = lib.tda_bwd_workspace_size(_lib.TDA_BF16, n_bh, S, D, int(norm))
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+    from tda_b200 import ops
+    status = ops._status_word(dev)
+
+    def bwd(qp, kp, gq, gk, scale, acc):
+        _lib.check(lib.tda_rect_bwd(qp, kp, ptr[-1], dout.data_ptr(), _lib.TDA_BF16, gq.data_ptr(), gk.data_ptr(),
+                                    grads[4].data_ptr(), n_bh, S, D, beta, p, int(norm), scale, acc,
+                                    ws.data_ptr(), ws_n, status.data_ptr(), sp))
 
     def step():
         if op == "diff":
-            _lib.check(lib.tda_rect_bwd(ptr[0], ptr[2], ptr[4], dout.data_ptr(), _lib.TDA_BF16, grads[0].data_ptr(),
-                                        grads[2].data_ptr(), grads[4].data_ptr(), n_bh, S, D, beta, p, int(norm),
-                                        1.0, 0, sp))
-            _lib.check(lib.tda_rect_bwd(ptr[1], ptr[3], ptr[4], dout.data_ptr(), _lib.TDA_BF16, grads[1].data_ptr(),
-                                        grads[3].data_ptr(), grads[4].data_ptr(), n_bh, S, D, beta, p, int(norm),
-                                        -lamc, 1, sp))
+            bwd(ptr[0], ptr[2], grads[0], grads[2], 1.0, 0)
+            bwd(ptr[1], ptr[3], grads[1], grads[3], -lamc, 1)
         else:
-            _lib.check(lib.tda_rect_bwd(ptr[0], ptr[1], ptr[2], dout.data_ptr(), _lib.TDA_BF16, grads[0].data_ptr(),
-                                        grads[1].data_ptr(), grads[2].data_ptr(), n_bh, S, D, beta, p, int(norm),
-                                        1.0, 0, sp))
+            bwd(ptr[0], ptr[1], grads[0], grads[1], 1.0, 0)
 
     for _ in range(args.warmup):
         step()
@@ -293,25 +296,24 @@ def run_tda_backward(args, rank, local, world):
     fl = bwd_flops(B * H, S, D, op == "diff")
     value = fl * args.steps / (ms / 1e3) / 1e12
     peaks, peak_src = load_peaks()
-    sm_mhz = float(peaks.get("sm_max_mhz", 1965.0))
-    fp32_peak = 148 * 128 * 2 * sm_mhz * 1e6 / 1e12  # nominal FFMA rate of the CUDA cores
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    ops.check_status(dev)
     achieved = bwd_flops(n_bh, S, D, op == "diff") * args.steps / (e0.elapsed_time(e1) / 1e3) / 1e12
     if rank == 0:
         line = {
             "metric": f"TDA backward TFLOP/s ({name})", "value": value, "unit": "TFLOP/s", "impl": "tda",
             "pass": "backward", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32 arithmetic on bf16 inputs", "data": "synthetic",
+            "dtype": "bf16", "data": "synthetic",
             "config": {"workload": describe(name) + " backward", "batch": B, "heads": H, "seq_len": S,
                        "head_dim": D, "flops_per_step": fl,
-                       "executed_flops_per_step": fl * 7.0 / 5.0,
-                       "kernels": "tda_bwd_dq_kernel + tda_bwd_dkv_kernel per branch (CUDA-core fp32)"},
-            "roofline": {"bound": "fp32 CUDA cores", "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
-                         "frac": achieved / fp32_peak, "traffic": None,
-                         "peak_source": "nominal: 148 SMs x 128 FP32 lanes x 2 x sm_max_mhz "
-                                        f"({sm_mhz:.0f} MHz, {peak_src} peaks file)"},
+                       "executed_flops_per_step_dense": fl * 8.0 / 5.0,
+                       "kernels": "key / query tables + tda_tc_bwd_dq_kernel + tda_tc_bwd_dkv_kernel per branch"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "peak_source": f"bf16_tflops (burst) of {peak_src}"},
             "cpu_baseline": None, "e2e": None,
-            "gpu_launches": (4 if op == "diff" else 2) * args.steps,
+            "gpu_launches": (8 if op == "diff" else 4) * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

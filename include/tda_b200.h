@@ -90,6 +90,11 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                  float lambda_param, float relu_power, int normalize, void* workspace, size_t workspace_bytes,
                  int* status, void* stream);
 
+/* Device workspace bytes needed by tda_rect_bwd for these sizes (0 on the
+ * CUDA-core path): the key table of k (normalize) and a per-query table of
+ * 1/||q_i|| and tau_i * ||q_i||. */
+size_t tda_bwd_workspace_size(int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, int normalize);
+
 /* Backward of one threshold rectified attention branch, given the upstream
  * gradient dout of its output (same shape and dtype as q):
  *   dq, dk, dv = gradients w.r.t. q, k, v of rect(q, k, v) for the gradient
@@ -102,12 +107,16 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
  * F.normalize'd inside and dq, dk are chained back through F.normalize (torch
  * autograd's part of :505-512).  accumulate_dv != 0 adds into dv (the
  * differential form calls this once per branch: dout_scale = 1, then
- * -clamp(lambda, 0, 1) with accumulate_dv = 1).  dtype: TDA_F32 or TDA_BF16
- * inputs; head_dim 16, 32, 64 or 128; exact fp32 arithmetic on CUDA cores.
+ * -clamp(lambda, 0, 1) with accumulate_dv = 1).
+ * bf16 inputs with head_dim 64 / 128 run on the tensor cores (tcgen05, bf16
+ * operands, P and dA as bf16 hi + lo, fp32 accumulation) and need the
+ * workspace (tda_bwd_workspace_size) and a device status word; fp32 inputs and
+ * head_dim 16 / 32 run exact fp32 on CUDA cores (workspace and status unused).
  * dq, dk, dv must not alias the inputs. */
 int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, int dtype, float* dq, float* dk,
                  float* dv, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,
-                 int normalize, float dout_scale, int accumulate_dv, void* stream);
+                 int normalize, float dout_scale, int accumulate_dv, void* workspace, size_t workspace_bytes,
+                 int* status, void* stream);
 
 /* Stage 1 of the normalized tensor-core path, exposed so callers can time or
  * reuse it.  Writes the key table of k into rk (batch_heads * pad * 17 / 16

@@ -263,9 +263,16 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                          relu_power, normalize, rk1, rk2, status, stream);
 }
 
+size_t tda_bwd_workspace_size(int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, int normalize) {
+  if (dtype != TDA_BF16 || (head_dim != 64 && head_dim != 128) || batch_heads < 1 || seq_len < 1) return 0;
+  const size_t keys = normalize ? (tda::key_table_floats(batch_heads, seq_len) * 4 + 255) / 256 * 256 : 0;
+  return keys + (tda::query_table_floats(batch_heads, seq_len) * 4 + 255) / 256 * 256;
+}
+
 int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, int dtype, float* dq, float* dk,
                  float* dv, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,
-                 int normalize, float dout_scale, int accumulate_dv, void* stream) {
+                 int normalize, float dout_scale, int accumulate_dv, void* workspace, size_t workspace_bytes,
+                 int* status, void* stream) {
   if (batch_heads < 1 || seq_len < 1)
     return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1 (got %lld, %lld)",
                 static_cast<long long>(batch_heads), static_cast<long long>(seq_len));
@@ -279,6 +286,49 @@ int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, 
   const void* ptrs[7] = {q, k, v, dout, dq, dk, dv};
   for (const void* ptr : ptrs)
     if (!ptr || !aligned16(ptr)) return fail(TDA_ERR_INVALID, "q, k, v, dout, dq, dk, dv must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == TDA_BF16 && (head_dim == 64 || head_dim == 128)) {
+    // tensor-core path: key table (normalize) and query table in the workspace
+    if (!status) return fail(TDA_ERR_INVALID, "status must point to a device int32");
+    const size_t need = tda_bwd_workspace_size(dtype, batch_heads, seq_len, head_dim, normalize);
+    if (!workspace || workspace_bytes < need)
+      return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+    const int BH = static_cast<int>(batch_heads), S = static_cast<int>(seq_len), D = static_cast<int>(head_dim);
+    const int S_pad = static_cast<int>(tda::padded_seq(seq_len));
+    const size_t key_bytes = normalize ? (tda::key_table_floats(batch_heads, seq_len) * 4 + 255) / 256 * 256 : 0;
+    float* rk = normalize ? static_cast<float*>(workspace) : nullptr;
+    float2* qc = reinterpret_cast<float2*>(static_cast<uint8_t*>(workspace) + key_bytes);
+    tda::TcBwdParams prm{};
+    int e;
+    if ((e = make_map(&prm.tm_q, q, batch_heads, seq_len, head_dim))) return e;
+    if ((e = make_map(&prm.tm_k, k, batch_heads, seq_len, head_dim))) return e;
+    if ((e = make_map(&prm.tm_v, v, batch_heads, seq_len, head_dim))) return e;
+    if ((e = make_map(&prm.tm_do, dout, batch_heads, seq_len, head_dim))) return e;
+    cudaError_t ce;
+    if (normalize && (ce = tda::launch_key_norms(k, 1, rk, BH, S, S_pad, D, st)) != cudaSuccess)
+      return cuda_fail(ce, "key table launch");
+    if ((ce = tda::launch_query_table(q, qc, BH, S, S_pad, D, beta, normalize, st)) != cudaSuccess)
+      return cuda_fail(ce, "query table launch");
+    prm.rk = rk;
+    prm.qc = qc;
+    prm.dq = dq;
+    prm.dk = dk;
+    prm.dv = dv;
+    prm.status = status;
+    prm.S = S;
+    prm.S_pad = S_pad;
+    prm.BH = BH;
+    prm.n_tiles = S_pad / tda::kTile;
+    prm.causal_skip = beta >= 0.0f ? 1 : 0;
+    prm.accumulate_dv = accumulate_dv ? 1 : 0;
+    prm.beta = beta;
+    prm.relu_power = relu_power;
+    prm.scale = dout_scale;
+    prm.timeout_ns = g_timeout_ns.load();
+    ce = tda::launch_tc_bwd(prm, D, normalize != 0, tda::pow_mode_of(relu_power), st);
+    if (ce != cudaSuccess) return cuda_fail(ce, "tensor-core backward launch");
+    return TDA_OK;
+  }
   tda::BwdParams prm{};
   prm.q = q;
   prm.k = k;
@@ -294,8 +344,7 @@ int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, 
   prm.dout_scale = dout_scale;
   prm.normalize = normalize ? 1 : 0;
   prm.accumulate_dv = accumulate_dv ? 1 : 0;
-  cudaError_t ce = tda::launch_rect_bwd(prm, static_cast<int>(head_dim), dtype == TDA_BF16,
-                                        static_cast<cudaStream_t>(stream));
+  cudaError_t ce = tda::launch_rect_bwd(prm, static_cast<int>(head_dim), dtype == TDA_BF16, st);
   if (ce != cudaSuccess) return cuda_fail(ce, "backward kernel launch");
   return TDA_OK;
 }

@@ -96,6 +96,39 @@ struct BwdParams {
 
 cudaError_t launch_rect_bwd(const BwdParams& p, int head_dim, bool in_bf16, cudaStream_t stream);
 
+// Tensor-core backward of one rectified branch (bf16 inputs, head_dim 64/128).
+// Tables (workspace): the key table of k (as for the forward) and a query
+// table qc[bh][i] = {rq_i, tq_i} (rq = 1/max(||q_i||,1e-12) or 1, tq = tau_i *
+// ||q_i|| or tau_i; rows past S: {0, +huge}).
+struct TcBwdParams {
+  CUtensorMap tm_q;
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  CUtensorMap tm_do;
+  const float* rk;   // key table of k
+  const float2* qc;  // query table
+  float* dq;
+  float* dk;
+  float* dv;
+  int* status;
+  int S;
+  int S_pad;
+  int BH;
+  int n_tiles;
+  int causal_skip;  // beta >= 0
+  int accumulate_dv;
+  float beta;
+  float relu_power;
+  float scale;      // dout_scale
+  unsigned long long timeout_ns;
+};
+
+// (S_pad per bh) query table floats: 2 per row
+inline size_t query_table_floats(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * padded_seq(S) * 2; }
+cudaError_t launch_query_table(const void* q, float2* qc, int BH, int S, int S_pad, int D, float beta, int normalize,
+                               cudaStream_t stream);
+cudaError_t launch_tc_bwd(const TcBwdParams& p, int head_dim, bool normalize, int pow_mode, cudaStream_t stream);
+
 // Key table of x: rk[bh][j] = 1 / max(||x[bh][j]||_2, 1e-12) for j < S, 0 for
 // S <= j < S_pad, followed by rkmax[bh][g] = max of rk over keys [16 g, 16 g + 16).
 inline size_t key_table_floats(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * padded_seq(S) / 16 * 17; }

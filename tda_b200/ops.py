@@ -191,12 +191,17 @@ def rect_backward(q, k, v, dout, beta, relu_power=2.0, normalize: bool = False, 
     if dq.numel() == 0:
         return dq, dk, dv
     lib = _lib.load()
+    ws_n = lib.tda_bwd_workspace_size(kind, B * H, S, D, int(normalize))
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=qc.device) if ws_n else None
     stream = torch.cuda.current_stream(qc.device).cuda_stream
     with torch.cuda.device(qc.device):
         rc = lib.tda_rect_bwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gc.data_ptr(), kind, dq.data_ptr(),
                               dk.data_ptr(), dv.data_ptr(), B * H, S, D, beta_v, p_v, int(normalize),
-                              float(dout_scale), int(accumulate), stream)
+                              float(dout_scale), int(accumulate), ws.data_ptr() if ws is not None else None, ws_n,
+                              _status_word(qc.device).data_ptr(), stream)
     _lib.check(rc)
+    if _SYNC_CHECK:
+        check_status(qc.device)
     return dq, dk, dv
 
 

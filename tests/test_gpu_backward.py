@@ -1,10 +1,13 @@
 """Backward pass of the CUDA path against the backward oracle, which is pinned
 to the reference's own gradients (tests/test_oracle_golden_bwd.py).
 
-The backward runs in exact fp32 on CUDA cores for fp32 and bf16 inputs, so:
-  * fp32 gradients (``rect_backward``) vs the fp64 oracle:          <= 1e-5 rel-L2
-  * through autograd, gradients in the inputs' dtype: fp32 <= 1e-5; bf16
-    gradients vs the bf16-rounded oracle                             <= 1e-3
+Paths and tolerances (rel-L2):
+  * fp32 inputs (and head_dim 16 / 32): exact fp32 on CUDA cores,
+    fp32 gradients vs the fp64 oracle                                <= 1e-5
+  * bf16 inputs, head_dim 64 / 128: tcgen05 tensor cores, bf16 operands with
+    P and dA as bf16 hi + lo, fp32 accumulation; fp32 gradients
+    (``rect_backward``) vs the fp64 oracle on the bf16 values         <= 2e-5
+  * through autograd, bf16 gradients vs the bf16-rounded oracle      <= 1e-3
 """
 import numpy as np
 import pytest
@@ -18,6 +21,7 @@ pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
 TOL_F32 = 1e-5
+TOL_TC = 2e-5
 TOL_BF16 = 1e-3
 
 
@@ -91,7 +95,7 @@ def test_rect_backward_bf16_inputs(D):
     dq, dk, dv = tda_b200.rect_backward(*(x.to(DEV) for x in (q, k, v, g)), 1.0, 2.0, True)
     ref = O.rect_bwd(*(x.float().numpy() for x in (q, k, v, g)), 1.0, 2.0, True)
     for got, r in zip((dq, dk, dv), ref):
-        assert O.rel_l2(_np(got), r) <= TOL_F32
+        assert O.rel_l2(_np(got), r) <= TOL_TC
     qg, kg, vg = (x.to(DEV).requires_grad_(True) for x in (q, k, v))
     out = tda_b200.threshold_rela_triton(qg, kg, vg, 1.0, 2.0, True)
     out.backward(g.to(DEV))
@@ -123,3 +127,31 @@ def test_backward_accumulates_dv():
     dv = dv1.clone()
     tda_b200.rect_backward(q, k, v, g, 1.0, 2.0, False, dout_scale=-0.5, dv=dv)
     assert O.rel_l2(_np(dv), 0.5 * _np(dv1)) <= 1e-6
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("shape_s,beta,p,norm", [(256, 1.0, 2.0, True), (200, 0.5, 3.0, False),
+                                                 (300, -0.5, 2.0, True), (256, 0.0, 1.0, True),
+                                                 (130, 1.5, 1.5, True), (129, -1.0, 2.0, False)])
+def test_tensor_core_backward_sweep(D, shape_s, beta, p, norm):
+    """The tcgen05 backward (bf16) over thresholds, powers, normalize, ragged
+    lengths and negative beta (masked entries kept in dQ / dK)."""
+    q, k, v, g = _gen(500 + shape_s + D, 4, (1, 2, shape_s, D), dtype=torch.bfloat16)
+    dq, dk, dv = tda_b200.rect_backward(*(x.to(DEV) for x in (q, k, v, g)), beta, p, norm)
+    tda_b200.check_status()
+    ref = O.rect_bwd(*(x.float().numpy() for x in (q, k, v, g)), beta, p, norm)
+    for got, r, name in zip((dq, dk, dv), ref, ("dq", "dk", "dv")):
+        assert O.rel_l2(_np(got), r) <= TOL_TC, (name, O.rel_l2(_np(got), r))
+
+
+def test_tensor_core_diff_backward_matches_oracle():
+    """Both branches of the differential form on the tensor cores (bf16, D 128)."""
+    xs = _gen(600, 6, (1, 2, 256, 128), dtype=torch.bfloat16)
+    ins = [x.to(DEV).requires_grad_(True) for x in xs[:5]]
+    lam = torch.tensor(0.6, device=DEV, requires_grad=True)
+    out = tda_b200.differential_threshold_rela_triton(*ins, 1.0, lam, 2.0, True)
+    out.backward(xs[5].to(DEV))
+    ref = O.diff_bwd(*(x.float().numpy() for x in xs[:5]), xs[5].float().numpy(), 1.0, 0.6, 2.0, True)
+    for t, r in zip(ins, ref[:5]):
+        assert O.rel_l2(_np(t.grad), O.bf16_round(r)) <= TOL_BF16
+    assert abs(float(lam.grad) - ref[5]) <= 2e-3 * max(1.0, abs(ref[5]))
