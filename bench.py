@@ -494,6 +494,9 @@ def run_tda(args, rank, local, world):
                f"inputs {in_bytes / 1e6:.0f} MB per GPU, not above the 126 MB L2")
     if rank == 0:
         traffic = MEASURED_TRAFFIC.get(name)
+        if traffic is not None and world > 1:
+            # measured at N = 1; a launch's DRAM bytes are proportional to the (batch, head) slices it covers
+            traffic = traffic * n_bh / (B * H)
         line = {
             "metric": METRIC,
             "value": value,
