@@ -118,6 +118,27 @@ int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, 
                  int normalize, float dout_scale, int accumulate_dv, void* workspace, size_t workspace_bytes,
                  int* status, void* stream);
 
+/* tda_rect_fwd / tda_diff_fwd for bf16 inputs given as strided
+ * (batch, heads, seq_len, head_dim) views with a contiguous last dimension,
+ * e.g. a (batch, seq_len, heads, head_dim) projection transposed to
+ * (batch, heads, seq_len, head_dim): the tensor maps and the key-norm pass
+ * read them in place (no copy).  strides: element strides (batch, head, seq)
+ * of each input in argument order (3 per input), positive multiples of 8;
+ * out is a contiguous (batch * heads, seq_len, head_dim) array.  head_dim 64 or
+ * 128.  Workspace as tda_workspace_size(differential, TDA_BF16, batch * heads,
+ * seq_len, head_dim, normalize).  Replaces the same reference entry points as
+ * tda_rect_fwd / tda_diff_fwd; the reference indexes such views with the
+ * (batch * heads) stride only (triton_threshold_attention.py:49-51), which is
+ * wrong for them. */
+int tda_rect_fwd_strided(const void* q, const void* k, const void* v, const int64_t* strides, void* out,
+                         int out_dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, float beta,
+                         float relu_power, int normalize, void* workspace, size_t workspace_bytes, int* status,
+                         void* stream);
+int tda_diff_fwd_strided(const void* q1, const void* q2, const void* k1, const void* k2, const void* v,
+                         const int64_t* strides, void* out, int out_dtype, int64_t batch, int64_t heads,
+                         int64_t seq_len, int64_t head_dim, float beta, float lambda_param, float relu_power,
+                         int normalize, void* workspace, size_t workspace_bytes, int* status, void* stream);
+
 /* Stage 1 of the normalized tensor-core path, exposed so callers can time or
  * reuse it.  Writes the key table of k into rk (batch_heads * pad * 17 / 16
  * floats, pad = seq_len rounded up to 128): rk[bh * pad + j] =

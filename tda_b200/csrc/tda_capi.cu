@@ -66,6 +66,32 @@ int make_map(CUtensorMap* m, const void* base, int64_t BH, int64_t S, int64_t D)
   return TDA_OK;
 }
 
+// A (batch, head, seq, dim) bf16 view: element strides of the first three
+// dimensions, the last one contiguous.
+struct View {
+  const void* p;
+  int64_t sb, sh, ss;
+};
+
+View contiguous_view(const void* p, int64_t BH, int64_t S, int64_t D) { return View{p, BH * S * D, S * D, D}; }
+
+// View viewed as 4-D {D, S, heads, batches}; box {64, 128, 1, 1}; 128-B swizzle.
+int make_map4(CUtensorMap* m, const View& x, int64_t batches, int64_t heads, int64_t S, int64_t D) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(batches)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(x.ss * 2), static_cast<cuuint64_t>(x.sh * 2),
+                           static_cast<cuuint64_t>(x.sb * 2)};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tda::kTile), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(x.p), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return TDA_OK;
+}
+
 int check_common(int64_t BH, int64_t S, int64_t D, int* status) {
   if (BH < 1 || S < 1) return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1 (got %lld, %lld)",
                                    static_cast<long long>(BH), static_cast<long long>(S));
@@ -80,15 +106,19 @@ int check_common(int64_t BH, int64_t S, int64_t D, int* status) {
 
 bool tc_supported(int dtype, int64_t D) { return dtype == TDA_BF16 && (D == 64 || D == 128); }
 
-int run_tc(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int out_dtype,
-           int64_t BH, int64_t S, int64_t D, float beta, float lam, float p, int normalize, const float* rk1,
-           const float* rk2, int* status, void* stream, bool differential) {
+int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const View& v, void* out, int out_dtype,
+           int64_t BH, int64_t heads, int64_t S, int64_t D, float beta, float lam, float p, int normalize,
+           const float* rk1, const float* rk2, int* status, void* stream, bool differential) {
   if (int e = check_common(BH, S, D, status)) return e;
+  if (heads < 1 || BH % heads != 0) return fail(TDA_ERR_INVALID, "heads must divide batch * heads");
   if (!(D == 64 || D == 128)) return fail(TDA_ERR_UNSUPPORTED, "tensor-core path needs head_dim 64 or 128");
   if (out_dtype != TDA_BF16 && out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "out_dtype must be TDA_BF16 or TDA_F32");
-  const void* ins[5] = {q1, k1, v, differential ? q2 : q1, differential ? k2 : k1};
-  for (const void* x : ins)
-    if (!x || !aligned16(x)) return fail(TDA_ERR_INVALID, "inputs must be non-NULL and 16-byte aligned");
+  const View* ins[5] = {&q1, &k1, &v, differential ? &q2 : &q1, differential ? &k2 : &k1};
+  for (const View* x : ins) {
+    if (!x->p || !aligned16(x->p)) return fail(TDA_ERR_INVALID, "inputs must be non-NULL and 16-byte aligned");
+    if (x->sb <= 0 || x->sh <= 0 || x->ss <= 0 || (x->sb | x->sh | x->ss) % 8 != 0)
+      return fail(TDA_ERR_INVALID, "input strides must be positive multiples of 8 elements (16 bytes)");
+  }
   if (!out || !aligned16(out)) return fail(TDA_ERR_INVALID, "out must be non-NULL and 16-byte aligned");
   if (normalize && (!rk1 || (differential && !rk2) || !aligned16(rk1) || (differential && !aligned16(rk2))))
     return fail(TDA_ERR_INVALID, "normalize needs 16-byte aligned key inverse norms");
@@ -97,12 +127,13 @@ int run_tc(const void* q1, const void* q2, const void* k1, const void* k2, const
   tda::TcFwdParams prm;
   std::memset(&prm, 0, sizeof(prm));
   int e;
-  if ((e = make_map(&prm.tm_q1, q1, BH, S, D))) return e;
-  if ((e = make_map(&prm.tm_k1, k1, BH, S, D))) return e;
-  if ((e = make_map(&prm.tm_v, v, BH, S, D))) return e;
+  const int64_t batches = BH / heads;
+  if ((e = make_map4(&prm.tm_q1, q1, batches, heads, S, D))) return e;
+  if ((e = make_map4(&prm.tm_k1, k1, batches, heads, S, D))) return e;
+  if ((e = make_map4(&prm.tm_v, v, batches, heads, S, D))) return e;
   if (differential) {
-    if ((e = make_map(&prm.tm_q2, q2, BH, S, D))) return e;
-    if ((e = make_map(&prm.tm_k2, k2, BH, S, D))) return e;
+    if ((e = make_map4(&prm.tm_q2, q2, batches, heads, S, D))) return e;
+    if ((e = make_map4(&prm.tm_k2, k2, batches, heads, S, D))) return e;
   }
   prm.rk1 = rk1;
   prm.rk2 = rk2;
@@ -111,6 +142,7 @@ int run_tc(const void* q1, const void* q2, const void* k1, const void* k2, const
   prm.S = static_cast<int>(S);
   prm.S_pad = static_cast<int>(tda::padded_seq(S));
   prm.BH = static_cast<int>(BH);
+  prm.heads = static_cast<int>(heads);
   prm.n_qtiles = static_cast<int>((S + tda::kTile - 1) / tda::kTile);
   prm.out_f32 = out_dtype == TDA_F32;
   prm.causal_skip = beta >= 0.0f ? 1 : 0;
@@ -199,16 +231,88 @@ int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq
 int tda_rect_fwd_tc(const void* q, const void* k, const void* v, void* out, int out_dtype, int64_t batch_heads,
                     int64_t seq_len, int64_t head_dim, float beta, float relu_power, int normalize,
                     const float* rk, int* status, void* stream) {
-  return run_tc(q, nullptr, k, nullptr, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, 0.0f, relu_power,
-                normalize, rk, nullptr, status, stream, false);
+  auto cv = [&](const void* x) { return contiguous_view(x, batch_heads, seq_len, head_dim); };
+  return run_tc(cv(q), cv(nullptr), cv(k), cv(nullptr), cv(v), out, out_dtype, batch_heads, batch_heads, seq_len,
+                head_dim, beta, 0.0f, relu_power, normalize, rk, nullptr, status, stream, false);
 }
 
 int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
                     int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta,
                     float lambda_param, float relu_power, int normalize, const float* rk1, const float* rk2,
                     int* status, void* stream) {
-  return run_tc(q1, q2, k1, k2, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, clamp01(lambda_param),
-                relu_power, normalize, rk1, rk2, status, stream, true);
+  auto cv = [&](const void* x) { return contiguous_view(x, batch_heads, seq_len, head_dim); };
+  return run_tc(cv(q1), cv(q2), cv(k1), cv(k2), cv(v), out, out_dtype, batch_heads, batch_heads, seq_len, head_dim,
+                beta, clamp01(lambda_param), relu_power, normalize, rk1, rk2, status, stream, true);
+}
+
+namespace {
+// Strided entry points: key tables of the strided keys, then the fused kernel.
+int run_strided(const View* views, int n, void* out, int out_dtype, int64_t batch, int64_t heads, int64_t S,
+                int64_t D, float beta, float lam, float p, int normalize, void* workspace, size_t workspace_bytes,
+                int* status, void* stream) {
+  const bool diff = n == 5;
+  if (batch < 1 || heads < 1) return fail(TDA_ERR_INVALID, "batch and heads must be >= 1");
+  if (!(D == 64 || D == 128))
+    return fail(TDA_ERR_UNSUPPORTED, "strided inputs run on the tensor-core path: head_dim 64 or 128 (got %lld)",
+                static_cast<long long>(D));
+  const int64_t BH = batch * heads;
+  if (int e = check_common(BH, S, D, status)) return e;
+  for (int i = 0; i < n; ++i)
+    if (views[i].sb <= 0 || views[i].sh <= 0 || views[i].ss <= 0 || (views[i].sb | views[i].sh | views[i].ss) % 8)
+      return fail(TDA_ERR_INVALID, "input strides must be positive multiples of 8 elements (16 bytes)");
+  // views: rect q, k, v; differential q1, q2, k1, k2, v
+  const View& q1 = views[0];
+  const View& q2 = diff ? views[1] : views[0];
+  const View& k1 = diff ? views[2] : views[1];
+  const View& k2 = diff ? views[3] : views[1];
+  const View& v = diff ? views[4] : views[2];
+  float* rk1 = nullptr;
+  float* rk2 = nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (normalize) {
+    const size_t need = tda_workspace_size(diff ? 1 : 0, TDA_BF16, BH, S, D, normalize);
+    if (!workspace || workspace_bytes < need) return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+    if (!aligned16(k1.p) || !aligned16(k2.p)) return fail(TDA_ERR_INVALID, "inputs must be 16-byte aligned");
+    rk1 = static_cast<float*>(workspace);
+    rk2 = diff ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2) : nullptr;
+    const int S_pad = static_cast<int>(tda::padded_seq(S));
+    cudaError_t ce = tda::launch_key_norms_strided(k1.p, rk1, static_cast<int>(BH), static_cast<int>(heads),
+                                                   static_cast<int>(S), S_pad, static_cast<int>(D), k1.sb, k1.sh,
+                                                   k1.ss, st);
+    if (ce == cudaSuccess && diff)
+      ce = tda::launch_key_norms_strided(k2.p, rk2, static_cast<int>(BH), static_cast<int>(heads),
+                                         static_cast<int>(S), S_pad, static_cast<int>(D), k2.sb, k2.sh, k2.ss, st);
+    if (ce != cudaSuccess) return cuda_fail(ce, "key table launch");
+  }
+  return run_tc(q1, q2, k1, k2, v, out, out_dtype, BH, heads, S, D, beta, lam, p, normalize, rk1, rk2, status, stream,
+                diff);
+}
+}  // namespace
+
+int tda_rect_fwd_strided(const void* q, const void* k, const void* v, const int64_t* strides, void* out,
+                         int out_dtype, int64_t batch, int64_t heads, int64_t seq_len, int64_t head_dim, float beta,
+                         float relu_power, int normalize, void* workspace, size_t workspace_bytes, int* status,
+                         void* stream) {
+  if (!strides) return fail(TDA_ERR_INVALID, "strides must point to 9 int64 values");
+  const View views[3] = {{q, strides[0], strides[1], strides[2]},
+                         {k, strides[3], strides[4], strides[5]},
+                         {v, strides[6], strides[7], strides[8]}};
+  return run_strided(views, 3, out, out_dtype, batch, heads, seq_len, head_dim, beta, 0.0f, relu_power, normalize,
+                     workspace, workspace_bytes, status, stream);
+}
+
+int tda_diff_fwd_strided(const void* q1, const void* q2, const void* k1, const void* k2, const void* v,
+                         const int64_t* strides, void* out, int out_dtype, int64_t batch, int64_t heads,
+                         int64_t seq_len, int64_t head_dim, float beta, float lambda_param, float relu_power,
+                         int normalize, void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  if (!strides) return fail(TDA_ERR_INVALID, "strides must point to 15 int64 values");
+  const View views[5] = {{q1, strides[0], strides[1], strides[2]},
+                         {q2, strides[3], strides[4], strides[5]},
+                         {k1, strides[6], strides[7], strides[8]},
+                         {k2, strides[9], strides[10], strides[11]},
+                         {v, strides[12], strides[13], strides[14]}};
+  return run_strided(views, 5, out, out_dtype, batch, heads, seq_len, head_dim, beta, clamp01(lambda_param),
+                     relu_power, normalize, workspace, workspace_bytes, status, stream);
 }
 
 int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dtype, int out_dtype,

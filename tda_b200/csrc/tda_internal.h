@@ -27,6 +27,10 @@ inline int64_t padded_seq(int64_t S) { return (S + kTile - 1) / kTile * kTile; }
 // Tensor-core (tcgen05) forward, bf16 storage.  q/k/v tensor maps view the
 // (batch*heads, S, D) arrays as 3-D {D, S, BH} with a {64, 128, 1} box and
 // 128-byte swizzle.
+// The forward kernel's tensor maps are 4-D {D, S, heads, batches}: a
+// (batch, head) index bh is loaded at (bh % heads, bh / heads), so strided
+// (batch, head, seq, dim) views (e.g. a (B, S, H, D) tensor transposed) need
+// no copy; a contiguous (BH, S, D) array is heads = BH, batches = 1.
 struct TcFwdParams {
   CUtensorMap tm_q1;
   CUtensorMap tm_q2;  // differential only
@@ -40,6 +44,7 @@ struct TcFwdParams {
   int S;
   int S_pad;
   int BH;
+  int heads;          // heads per batch in the tensor maps
   int n_qtiles;
   int out_f32;
   int causal_skip;    // 1 when beta >= 0: key tiles past the diagonal contribute 0
@@ -134,6 +139,10 @@ cudaError_t launch_tc_bwd(const TcBwdParams& p, int head_dim, bool normalize, in
 inline size_t key_table_floats(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * padded_seq(S) / 16 * 17; }
 cudaError_t launch_key_norms(const void* x, int x_is_bf16, float* rk, int BH, int S, int S_pad, int D,
                              cudaStream_t stream);
+// Same for a strided (batch, head, seq, dim) view (strides in elements, last
+// dimension contiguous); bh = b * heads + h.
+cudaError_t launch_key_norms_strided(const void* x, float* rk, int BH, int heads, int S, int S_pad, int D,
+                                     int64_t stride_b, int64_t stride_h, int64_t stride_s, cudaStream_t stream);
 
 // Sets the thread-local message returned by tda_last_error().
 void set_last_error(const char* msg);

@@ -1,4 +1,5 @@
-// Key-norm pre-pass for the normalized tensor-core path.  For one key tensor
+// Key-norm pre-pass for the normalized tensor-core path (any (batch, head,
+// seq, dim) strides with a contiguous last dimension).  For one key tensor
 // it writes a "key table" of BH * S_pad * 17/16 floats:
 //   rk[bh * S_pad + j]              = 1 / max(||k[bh][j]||_2, 1e-12)  (F.normalize
 //                                     eps, triton_threshold_attention.py:505-509),
@@ -15,9 +16,12 @@
 namespace tda {
 namespace {
 
+// x is a (batch, head, seq, dim) view with element strides (sb, sh, ss) and a
+// contiguous last dimension; bh = b * heads + h.
 template <int D>
 __global__ void __launch_bounds__(256) key_norm_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ table,
-                                                       int BH, int S, int S_pad) {
+                                                       int BH, int S, int S_pad, int heads, long long sb,
+                                                       long long sh, long long ss_) {
   constexpr int kRowBytes = D * 2;
   constexpr int kLanesPerRow = kRowBytes / 16;       // 16 (D = 128) or 8 (D = 64)
   constexpr int kRowsPerIter = 32 / kLanesPerRow;    // 2 or 4
@@ -31,13 +35,14 @@ __global__ void __launch_bounds__(256) key_norm_kernel(const __nv_bfloat16* __re
   for (long long g = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; g < groups; g += n_warps) {
     const int bh = static_cast<int>(g / (S_pad / 16));
     const int j0 = static_cast<int>(g % (S_pad / 16)) * 16;
+    const __nv_bfloat16* xb = x + static_cast<long long>(bh / heads) * sb + static_cast<long long>(bh % heads) * sh;
     float mx = 0.0f;
 #pragma unroll
     for (int it = 0; it < kIters; ++it) {
       const int j = j0 + it * kRowsPerIter + sub;
       float ss = 0.0f;
       if (j < S) {
-        const uint4 u = reinterpret_cast<const uint4*>(x + (static_cast<size_t>(bh) * S + j) * D)[sl];
+        const uint4 u = reinterpret_cast<const uint4*>(xb + static_cast<long long>(j) * ss_)[sl];
         const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
@@ -59,7 +64,8 @@ __global__ void __launch_bounds__(256) key_norm_kernel(const __nv_bfloat16* __re
 }
 
 template <int D>
-cudaError_t launch_kn(const void* x, float* table, int BH, int S, int S_pad, cudaStream_t stream) {
+cudaError_t launch_kn(const void* x, float* table, int BH, int S, int S_pad, int heads, long long sb, long long sh,
+                      long long ss, cudaStream_t stream) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -69,7 +75,7 @@ cudaError_t launch_kn(const void* x, float* table, int BH, int S, int S_pad, cud
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   key_norm_kernel<D><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), table,
-                                                                         BH, S, S_pad);
+                                                                         BH, S, S_pad, heads, sb, sh, ss);
   return cudaGetLastError();
 }
 
@@ -78,9 +84,18 @@ cudaError_t launch_kn(const void* x, float* table, int BH, int S, int S_pad, cud
 cudaError_t launch_key_norms(const void* x, int x_is_bf16, float* rk, int BH, int S, int S_pad, int D,
                              cudaStream_t stream) {
   if (x_is_bf16) {
-    if (D == 64) return launch_kn<64>(x, rk, BH, S, S_pad, stream);
-    if (D == 128) return launch_kn<128>(x, rk, BH, S, S_pad, stream);
+    // contiguous (BH, S, D): one "batch" of BH heads
+    const long long sh = static_cast<long long>(S) * D;
+    if (D == 64) return launch_kn<64>(x, rk, BH, S, S_pad, BH, sh * BH, sh, D, stream);
+    if (D == 128) return launch_kn<128>(x, rk, BH, S, S_pad, BH, sh * BH, sh, D, stream);
   }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_key_norms_strided(const void* x, float* rk, int BH, int heads, int S, int S_pad, int D,
+                                     int64_t stride_b, int64_t stride_h, int64_t stride_s, cudaStream_t stream) {
+  if (D == 64) return launch_kn<64>(x, rk, BH, S, S_pad, heads, stride_b, stride_h, stride_s, stream);
+  if (D == 128) return launch_kn<128>(x, rk, BH, S, S_pad, heads, stride_b, stride_h, stride_s, stream);
   return cudaErrorInvalidValue;
 }
 

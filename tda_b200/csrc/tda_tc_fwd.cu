@@ -127,14 +127,15 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
   uint8_t* ring = smem + C::kOffRing;
   float* rk_s = reinterpret_cast<float*>(smem + C::kOffRk);
   const int q0 = qt * kTile;
+  const int h_idx = bh % p.heads, b_idx = bh / p.heads;  // tensor-map coordinates of this (batch, head)
   bool q_issued = false;
   if (!(p.inject & 1)) {
     mbar_arrive_expect_tx(&bars->q_full, C::kNQ * C::kTileBytes);
 #pragma unroll
     for (int b = 0; b < C::kBoxes; ++b) {
-      tma_load_3d(smem + b * C::kBoxBytes, &p.tm_q1, &bars->q_full, b * 64, q0, bh);
+      tma_load_4d(smem + b * C::kBoxBytes, &p.tm_q1, &bars->q_full, b * 64, q0, h_idx, b_idx);
       if constexpr (DIFF)
-        tma_load_3d(smem + C::kTileBytes + b * C::kBoxBytes, &p.tm_q2, &bars->q_full, b * 64, q0, bh);
+        tma_load_4d(smem + C::kTileBytes + b * C::kBoxBytes, &p.tm_q2, &bars->q_full, b * 64, q0, h_idx, b_idx);
     }
     q_issued = true;
   }
@@ -153,7 +154,8 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
     mbar_arrive_expect_tx(&bars->slot_full[slot], C::kTileBytes);
     uint8_t* dst = ring + slot * C::kTileBytes;
 #pragma unroll
-    for (int b = 0; b < C::kBoxes; ++b) tma_load_3d(dst + b * C::kBoxBytes, map, &bars->slot_full[slot], b * 64, j * kTile, bh);
+    for (int b = 0; b < C::kBoxes; ++b)
+      tma_load_4d(dst + b * C::kBoxBytes, map, &bars->slot_full[slot], b * 64, j * kTile, h_idx, b_idx);
     ++ridx;
   };
   auto load_rk = [&](int j) {

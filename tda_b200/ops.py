@@ -101,6 +101,43 @@ def _finish(out: torch.Tensor, orig: torch.dtype, out_dtype) -> torch.Tensor:
     return out
 
 
+def _strided_eligible(ts) -> bool:
+    """bf16 CUDA views the tensor-core kernel can read in place: same device,
+    contiguous last dimension, head_dim 64 / 128, element strides of the first
+    three dimensions positive multiples of 8, 16-byte aligned data."""
+    t0 = ts[0]
+    if t0.dim() != 4 or t0.shape[-1] not in (64, 128) or not t0.is_cuda:
+        return False
+    for t in ts:
+        if t.dtype != torch.bfloat16 or t.device != t0.device or t.stride(-1) != 1 or t.data_ptr() % 16:
+            return False
+        if any(x <= 0 or x % 8 for x in t.stride()[:3]):
+            return False
+    return not all(t.is_contiguous() for t in ts)
+
+
+def _strided_call(entry, ts, out_dtype, extra, normalize, differential):
+    import ctypes
+    B, H, S, D = ts[0].shape
+    raw_dt = torch.float32 if out_dtype == torch.float32 else torch.bfloat16
+    out = torch.empty((B, H, S, D), dtype=raw_dt, device=ts[0].device)
+    if out.numel() == 0:
+        return out
+    lib = _lib.load()
+    ws_n = lib.tda_workspace_size(int(differential), _lib.TDA_BF16, B * H, S, D, int(normalize))
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=out.device) if ws_n else None
+    strides = (ctypes.c_int64 * (3 * len(ts)))(*[x for t in ts for x in t.stride()[:3]])
+    out_kind = _lib.TDA_F32 if raw_dt == torch.float32 else _lib.TDA_BF16
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    with torch.cuda.device(out.device):
+        rc = getattr(lib, entry)(*[t.data_ptr() for t in ts], ctypes.cast(strides, ctypes.c_void_p),
+                                 out.data_ptr(), out_kind, B, H, S, D, *extra, int(normalize),
+                                 ws.data_ptr() if ws is not None else None, ws_n,
+                                 _status_word(out.device).data_ptr(), stream)
+    _lib.check(rc)
+    return out
+
+
 def rect_forward(q, k, v, beta, relu_power=2.0, normalize: bool = False, out_dtype=None) -> torch.Tensor:
     """Threshold rectified attention forward (no autograd).  ``out_dtype``
     (default: q's dtype) may be torch.float32 on the bf16 path to receive the
@@ -109,6 +146,10 @@ def rect_forward(q, k, v, beta, relu_power=2.0, normalize: bool = False, out_dty
     assert q.shape == k.shape == v.shape
     beta_v = _scalar(beta)
     p_v = _scalar(relu_power)
+    if _strided_eligible([q, k, v]):
+        # strided views (e.g. (B, S, H, D) transposed) are read in place
+        out = _strided_call("tda_rect_fwd_strided", [q, k, v], out_dtype, (beta_v, p_v), normalize, False)
+        return _finish(out, q.dtype, out_dtype)
     kind, (qc, kc, vc), orig = _plan([q, k, v], "threshold_rela_triton")
     B, H, S, D = qc.shape
     raw_dt = torch.float32 if (kind == _lib.TDA_F32 or out_dtype == torch.float32) else torch.bfloat16
@@ -143,6 +184,10 @@ def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normaliz
         lam = torch.clamp(lambda_param.to(device=o1.device, dtype=torch.float32), min=0.0, max=1.0)
         return _finish(o1 - lam * o2, q1.dtype, out_dtype)
     lam_v = _scalar(lambda_param)
+    if _strided_eligible([q1, q2, k1, k2, v]):
+        out = _strided_call("tda_diff_fwd_strided", [q1, q2, k1, k2, v], out_dtype, (beta_v, lam_v, p_v), normalize,
+                            True)
+        return _finish(out, q1.dtype, out_dtype)
     kind, (a, b, c, d, e), orig = _plan([q1, q2, k1, k2, v], "differential_threshold_rela_triton")
     B, H, S, D = a.shape
     raw_dt = torch.float32 if (kind == _lib.TDA_F32 or out_dtype == torch.float32) else torch.bfloat16
