@@ -22,6 +22,7 @@ of the reference (oracle/) on the host cores instead.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -51,6 +52,9 @@ WORKLOADS = {
     "rect2k": ("rect", 4, 32, 2048, 128, 1.0, 0.0, 2.0, True),
     "diff_s8k": ("diff", 2, 8, 8192, 128, 1.0, 0.5, 2.0, True),
     "rect_s8k": ("rect", 4, 8, 8192, 128, 1.0, 0.0, 2.0, True),
+    # BASELINE config 5's shape (parameter sweep), beta=1 p=2 normalized; with --dtype f32 the
+    # exact-fp32 CUDA-core path
+    "sweep2k": ("rect", 2, 16, 2048, 64, 1.0, 0.0, 2.0, True),
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one main-kernel launch,
@@ -250,9 +254,11 @@ def run_tda_backward(args, rank, local, world):
     name = args.config
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
     shard = shard_range(B * H, world, rank)
-    xs = make_inputs(name, shard, dev)
+    f32 = args.dtype == "f32"
+    kind = _lib.TDA_F32 if f32 else _lib.TDA_BF16
+    xs = make_inputs(name, shard, dev, "bhsd", args.dtype)
     g = torch.Generator(device=dev).manual_seed(777 + shard.start)
-    dout = torch.randn(xs[0].shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    dout = torch.randn(xs[0].shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16).to(xs[0].dtype)
     n_bh = shard.size
     lib = _lib.load()
     grads = [torch.empty(xs[0].shape, dtype=torch.float32, device=dev) for _ in range(5)]
@@ -260,13 +266,13 @@ def run_tda_backward(args, rank, local, world):
     sp = stream.cuda_stream
     ptr = [x.data_ptr() for x in xs]
     lamc = min(max(lam, 0.0), 1.0)
-    ws_n = lib.tda_bwd_workspace_size(_lib.TDA_BF16, n_bh, S, D, int(norm))
+    ws_n = lib.tda_bwd_workspace_size(kind, n_bh, S, D, int(norm))
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
     from tda_b200 import ops
     status = ops._status_word(dev)
 
     def bwd(qp, kp, gq, gk, scale, acc):
-        _lib.check(lib.tda_rect_bwd(qp, kp, ptr[-1], dout.data_ptr(), _lib.TDA_BF16, gq.data_ptr(), gk.data_ptr(),
+        _lib.check(lib.tda_rect_bwd(qp, kp, ptr[-1], dout.data_ptr(), kind, gq.data_ptr(), gk.data_ptr(),
                                     grads[4].data_ptr(), n_bh, S, D, beta, p, int(norm), scale, acc,
                                     ws.data_ptr(), ws_n, status.data_ptr(), sp))
 
@@ -297,6 +303,10 @@ def run_tda_backward(args, rank, local, world):
     value = fl * args.steps / (ms / 1e3) / 1e12
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak_note = f"bf16_tflops (burst) of {peak_src}"
+    if f32:
+        peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        peak_note = "nominal FFMA peak, 148 SMs x 128 lanes x 2 x 1.965 GHz"
     ops.check_status(dev)
     achieved = bwd_flops(n_bh, S, D, op == "diff") * args.steps / (e0.elapsed_time(e1) / 1e3) / 1e12
     if rank == 0:
@@ -304,16 +314,16 @@ def run_tda_backward(args, rank, local, world):
             "metric": f"TDA backward TFLOP/s ({name})", "value": value, "unit": "TFLOP/s", "impl": "tda",
             "pass": "backward", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": describe(name) + " backward", "batch": B, "heads": H, "seq_len": S,
+            "dtype": "f32" if f32 else "bf16", "data": "synthetic",
+            "config": {"workload": describe(name) + (", fp32 inputs (CUDA-core path)" if f32 else "") + " backward", "batch": B, "heads": H, "seq_len": S,
                        "head_dim": D, "flops_per_step": fl,
                        "executed_flops_per_step_dense": fl * 8.0 / 5.0,
-                       "kernels": "key / query tables + tda_tc_bwd_dq_kernel + tda_tc_bwd_dkv_kernel per branch"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "peak_source": f"bf16_tflops (burst) of {peak_src}"},
+                       "kernels": "tda_bwd_dq_kernel + tda_bwd_dkv_kernel per branch" if f32 else
+                       "key / query tables + tda_tc_bwd_dq_kernel + tda_tc_bwd_dkv_kernel per branch"},
+            "roofline": {"bound": "fp32-fma" if f32 else "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None, "peak_source": peak_note},
             "cpu_baseline": None, "e2e": None,
-            "gpu_launches": (8 if op == "diff" else 4) * args.steps,
+            "gpu_launches": (2 if f32 else 4) * (2 if op == "diff" else 1) * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -323,15 +333,22 @@ def run_tda_backward(args, rank, local, world):
 
 
 # ------------------------------------------------------------------- GPU arm
-def make_inputs(name, shard, device):
+def make_inputs(name, shard, device, layout="bhsd", dtype="bf16"):
     """Seeded N(0,1) inputs per (tensor, flattened head): identical data for a
-    given head whatever the number of ranks."""
+    given head whatever the number of ranks.  layout "bshd" stores each tensor
+    as (1, S, heads, D) and returns the (1, heads, S, D) transposed view, the
+    layout of a fused QKV projection that the strided entry points read in
+    place; dtype "f32" keeps the same values in fp32."""
     import torch
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
     n = 5 if op == "diff" else 3
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
     xs = []
     for t in range(n):
-        x = torch.empty((1, shard.size, S, D), dtype=torch.bfloat16, device=device)
+        if layout == "bshd":
+            x = torch.empty((1, S, shard.size, D), dtype=tdt, device=device).transpose(1, 2)
+        else:
+            x = torch.empty((1, shard.size, S, D), dtype=tdt, device=device)
         for i, bh in enumerate(range(shard.start, shard.stop)):
             g = torch.Generator(device=device).manual_seed(1_000_003 * (t + 1) + bh)
             x[0, i] = torch.randn((S, D), generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
@@ -361,25 +378,46 @@ def run_tda(args, rank, local, world):
     name = args.config
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
     shard = shard_range(B * H, world, rank)
-    xs = make_inputs(name, shard, dev)
+    xs = make_inputs(name, shard, dev, args.layout, args.dtype)
     n_bh = shard.size
     lib = _lib.load()
     status = ops._status_word(dev)
     S_pad = (S + 127) // 128 * 128
-    out = torch.empty((1, n_bh, S, D), dtype=torch.bfloat16, device=dev)
+    f32 = args.dtype == "f32"
+    strided = args.layout == "bshd"
+    out = torch.empty((1, n_bh, S, D), dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
     rk = [torch.zeros(n_bh * S_pad // 16 * 17, dtype=torch.float32, device=dev) for _ in range(2)]  # key tables
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
     ptr = [x.data_ptr() for x in xs]
 
+    # the fp32 path computes the norms inside its kernel; the strided entries
+    # run their key-norm pre-pass inside the call (timed with the main kernel)
+    separate_norms = norm and not f32 and not strided
+    ws_n = lib.tda_workspace_size(int(op == "diff"), _lib.TDA_BF16, n_bh, S, D, int(norm)) if strided else 0
+    ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
+    strides = (ctypes.c_int64 * (3 * len(xs)))(*[st for x in xs for st in x.stride()[:3]])
+
     def launch_norms():
-        if norm:
+        if separate_norms:
             ks = (ptr[2], ptr[3]) if op == "diff" else (ptr[1],)
             for kp, r in zip(ks, rk):
                 _lib.check(lib.tda_key_inv_norms(kp, _lib.TDA_BF16, n_bh, S, D, r.data_ptr(), sp))
 
     def launch_main():
-        if op == "diff":
+        if f32:
+            if op == "diff":
+                _lib.check(lib.tda_diff_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, n_bh, S, D, beta, lam,
+                                            p, int(norm), None, 0, status.data_ptr(), sp))
+            else:
+                _lib.check(lib.tda_rect_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, n_bh, S, D, beta, p,
+                                            int(norm), None, 0, status.data_ptr(), sp))
+        elif strided:
+            fn = lib.tda_diff_fwd_strided if op == "diff" else lib.tda_rect_fwd_strided
+            extra = (beta, lam, p) if op == "diff" else (beta, p)
+            _lib.check(fn(*ptr, ctypes.cast(strides, ctypes.c_void_p), out.data_ptr(), _lib.TDA_BF16, 1, n_bh, S,
+                          D, *extra, int(norm), ws.data_ptr(), ws_n, status.data_ptr(), sp))
+        elif op == "diff":
             _lib.check(lib.tda_diff_fwd_tc(ptr[0], ptr[1], ptr[2], ptr[3], ptr[4], out.data_ptr(), _lib.TDA_BF16,
                                            n_bh, S, D, beta, lam, p, int(norm), rk[0].data_ptr(),
                                            rk[1].data_ptr(), status.data_ptr(), sp))
@@ -387,7 +425,7 @@ def run_tda(args, rank, local, world):
             _lib.check(lib.tda_rect_fwd_tc(ptr[0], ptr[1], ptr[2], out.data_ptr(), _lib.TDA_BF16, n_bh, S, D, beta,
                                            p, int(norm), rk[0].data_ptr(), status.data_ptr(), sp))
 
-    launches_per_step = (2 if op == "diff" else 1) * int(norm) + 1
+    launches_per_step = (2 if op == "diff" else 1) * int(norm and not f32) + 1
 
     for _ in range(args.warmup):
         launch_norms()
@@ -421,10 +459,17 @@ def run_tda(args, rank, local, world):
     value = flops_total * args.steps / (total_ms_max / 1e3) / 1e12
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    peak_note = f"bf16_tflops (burst) of {peak_src}"
+    if f32:
+        # FFMA: 148 SMs x 128 FMA lanes x 2 FLOP x 1.965 GHz (nominal; no measured fp32 figure)
+        peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        peak_note = "nominal FFMA peak, 148 SMs x 128 lanes x 2 x 1.965 GHz"
     achieved = flops_of(op, n_bh, S, D) / (main_avg / 1e3) / 1e12  # this rank's launch
 
     # ---- end to end through the public API with pinned host buffers
-    host_in = [x.cpu().pin_memory() for x in xs]
+    # host copies keep the device layout (the storage of a bshd view)
+    stor = [x.transpose(1, 2) if strided else x for x in xs]
+    host_in = [x.cpu().pin_memory() for x in stor]
     host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     h2d = sum(x.numel() * x.element_size() for x in host_in)
     d2h = host_out.numel() * host_out.element_size()
@@ -435,8 +480,9 @@ def run_tda(args, rank, local, world):
     # chunk c (compute stream) and device->host copy of chunk c-1 (second copy
     # engine) overlap.  Every byte of every input and of the output crosses
     # PCIe inside the timed region.
-    dev_in = [torch.empty_like(x) for x in xs]
-    n_chunks = min(n_bh, 8)
+    dev_in = [torch.empty_like(x) for x in stor]
+    # a chunk of heads of a bshd tensor is not one block of memory: copy it whole
+    n_chunks = 1 if strided else min(n_bh, 8)
     bounds = [(c * n_bh // n_chunks, (c + 1) * n_bh // n_chunks) for c in range(n_chunks)]
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
@@ -449,13 +495,16 @@ def run_tda(args, rank, local, world):
         with torch.cuda.stream(s_in):
             for a, b in bounds:
                 for hbuf, dbuf in zip(host_in, dev_in):
-                    dbuf[:, a:b].copy_(hbuf[:, a:b], non_blocking=True)
+                    if strided:
+                        dbuf.copy_(hbuf, non_blocking=True)
+                    else:
+                        dbuf[:, a:b].copy_(hbuf[:, a:b], non_blocking=True)
                 e = torch.cuda.Event()
                 e.record(s_in)
                 ready.append(e)
         for (a, b), e in zip(bounds, ready):
             stream.wait_event(e)
-            d = [x[:, a:b] for x in dev_in]
+            d = [x.transpose(1, 2) if strided else x[:, a:b] for x in dev_in]
             if op == "diff":
                 o = tda_b200.differential_threshold_rela_triton(*d, betat, lamt, p, norm)
             else:
@@ -489,11 +538,11 @@ def run_tda(args, rank, local, world):
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
 
     n_inputs = 5 if op == "diff" else 3
-    in_bytes = n_inputs * B * H * S * D * 2 // world
+    in_bytes = n_inputs * B * H * S * D * (4 if f32 else 2) // world
     l2_note = (f"inputs {in_bytes / 1e9:.2f} GB per GPU > 126 MB L2; no flush" if in_bytes > 126e6 else
                f"inputs {in_bytes / 1e6:.0f} MB per GPU, not above the 126 MB L2")
     if rank == 0:
-        traffic = MEASURED_TRAFFIC.get(name)
+        traffic = None if (f32 or strided) else MEASURED_TRAFFIC.get(name)
         if traffic is not None and world > 1:
             # measured at N = 1; a launch's DRAM bytes are proportional to the (batch, head) slices it covers
             traffic = traffic * n_bh / (B * H)
@@ -509,11 +558,14 @@ def run_tda(args, rank, local, world):
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "f32" if f32 else "bf16",
             "data": "synthetic",
-            "pct_bf16_peak": value / world / peak,
+            "pct_bf16_peak": None if f32 else value / world / peak,
             "config": {
-                "workload": describe(name),
+                "workload": describe(name) + (", fp32 inputs (CUDA-core path)" if f32 else "")
+                + (", (B, S, H, D) storage read in place through the strided entry (main_kernel_ms includes "
+                   "its key-norm pre-pass)" if strided else ""),
+                "layout": args.layout,
                 "batch": B, "heads": H, "seq_len": S, "head_dim": D,
                 "parallelism": f"(batch x head) shards over {world} GPU(s), no collective on the data path",
                 "flops_per_step": flops_total,
@@ -523,13 +575,13 @@ def run_tda(args, rank, local, world):
                 "main_kernel_ms_max_rank": main_avg_max,
             },
             "roofline": {
-                "bound": "tensor",
+                "bound": "fp32-fma" if f32 else "tensor",
                 "achieved": achieved,
                 "peak": peak,
                 "unit": "TFLOP/s",
                 "frac": achieved / peak,
                 "traffic": traffic,
-                "peak_source": f"bf16_tflops (burst) of {peak_src}",
+                "peak_source": peak_note,
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "TFLOP/s",
@@ -556,6 +608,10 @@ def main():
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="diff8k")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layout", choices=["bhsd", "bshd"], default="bhsd",
+                    help="bshd: (B, S, H, D) storage passed as transposed views (strided entry points)")
+    ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
+                    help="f32: fp32 inputs on the exact-fp32 CUDA-core path")
     ap.add_argument("--backward", action="store_true",
                     help="time the backward pass of the workload instead of the forward")
     ap.add_argument("--ref-rows", type=int, default=256, help="query rows per reference-arm step")
