@@ -66,6 +66,24 @@ int make_map(CUtensorMap* m, const void* base, int64_t BH, int64_t S, int64_t D)
   return TDA_OK;
 }
 
+// The forward output, contiguous (BH, S, D) bf16 or f32, as 3-D {D, S, BH};
+// box {128 bytes of elements, 128 rows, 1}, 128-B swizzle (the layout the
+// epilogue stages each 128-row tile in before its TMA store).
+int make_out_map(CUtensorMap* m, void* out, bool f32, int64_t BH, int64_t S, int64_t D) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int64_t es = f32 ? 4 : 2;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * es), static_cast<cuuint64_t>(S * D * es)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(tda::kTile), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return TDA_OK;
+}
+
 // A (batch, head, seq, dim) bf16 view: element strides of the first three
 // dimensions, the last one contiguous.
 struct View {
@@ -135,6 +153,7 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
     if ((e = make_map4(&prm.tm_q2, q2, batches, heads, S, D))) return e;
     if ((e = make_map4(&prm.tm_k2, k2, batches, heads, S, D))) return e;
   }
+  if ((e = make_out_map(&prm.tm_out, out, out_dtype == TDA_F32, BH, S, D))) return e;
   prm.rk1 = rk1;
   prm.rk2 = rk2;
   prm.out = out;

@@ -37,6 +37,7 @@ struct TcFwdParams {
   CUtensorMap tm_k1;
   CUtensorMap tm_k2;  // differential only
   CUtensorMap tm_v;
+  CUtensorMap tm_out;  // out, contiguous (BH, S, D) as 3-D {D, S, BH}: box {128 B of elements, 128, 1}, 128-B swizzle
   const float* rk1;   // key table of k1 (normalize only): rk [BH][S_pad] then rkmax [BH][S_pad/16]
   const float* rk2;   // same for k2 (differential + normalize)
   void* out;          // [BH][S][D], bf16 or f32 (out_f32)

@@ -120,28 +120,60 @@ struct Bars {
 static_assert(sizeof(Bars) <= 1024, "barrier block too large");
 
 // ------------------------------------------------------------------ producer
+// The first copies of a CTA: the query tile(s), key tile 0 (K1_0 and K2_0
+// for the differential form) into ring slots 0 (and 1), and key-table entry
+// 0.  Issued by the thread that initialised the barriers, before the CTA-wide
+// barrier, so their latency overlaps the TMEM allocation and the start-up of
+// the other warps; every barrier they use is fresh, so nothing waits.
+template <int D, bool DIFF, bool NORM>
+__device__ void issue_first_loads(const TcFwdParams& p, uint8_t* smem, Bars* bars, int bh, int qt) {
+  using C = Cfg<D, DIFF>;
+  const int h_idx = bh % p.heads, b_idx = bh / p.heads;  // tensor-map coordinates of this (batch, head)
+  if (!(p.inject & 1)) {
+    mbar_arrive_expect_tx(&bars->q_full, C::kNQ * C::kTileBytes);
+#pragma unroll
+    for (int b = 0; b < C::kBoxes; ++b) {
+      tma_load_4d(smem + b * C::kBoxBytes, &p.tm_q1, &bars->q_full, b * 64, qt * kTile, h_idx, b_idx);
+      if constexpr (DIFF)
+        tma_load_4d(smem + C::kTileBytes + b * C::kBoxBytes, &p.tm_q2, &bars->q_full, b * 64, qt * kTile, h_idx,
+                    b_idx);
+    }
+  }
+  if constexpr (NORM) {
+    float* dst = reinterpret_cast<float*>(smem + C::kOffRk);
+    constexpr int kNB = DIFF ? 2 : 1;
+    mbar_arrive_expect_tx(&bars->rk_full[0], C::kRkPerTile * 4);
+    const size_t off = static_cast<size_t>(bh) * p.S_pad;
+    const size_t moff = static_cast<size_t>(p.BH) * p.S_pad + static_cast<size_t>(bh) * (p.S_pad / 16);
+    bulk_load(dst, p.rk1 + off, kTile * 4, &bars->rk_full[0]);
+    if constexpr (DIFF) bulk_load(dst + kTile, p.rk2 + off, kTile * 4, &bars->rk_full[0]);
+    bulk_load(dst + kNB * kTile, p.rk1 + moff, 32, &bars->rk_full[0]);
+    if constexpr (DIFF) bulk_load(dst + kNB * kTile + 8, p.rk2 + moff, 32, &bars->rk_full[0]);
+  }
+  constexpr int kFirst = DIFF ? 2 : 1;
+#pragma unroll
+  for (int t = 0; t < kFirst; ++t) {
+    const CUtensorMap* map = t == 0 ? &p.tm_k1 : &p.tm_k2;
+    mbar_arrive_expect_tx(&bars->slot_full[t], C::kTileBytes);
+    uint8_t* dst = smem + C::kOffRing + t * C::kTileBytes;
+#pragma unroll
+    for (int b = 0; b < C::kBoxes; ++b)
+      tma_load_4d(dst + b * C::kBoxBytes, map, &bars->slot_full[t], b * 64, 0, h_idx, b_idx);
+  }
+}
+
+// Every later copy, in consumption order, after issue_first_loads.
 template <int D, bool DIFF, bool NORM>
 __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, const WaitCtl& ctl, int bh, int qt,
                              int n_kt) {
   using C = Cfg<D, DIFF>;
   uint8_t* ring = smem + C::kOffRing;
   float* rk_s = reinterpret_cast<float*>(smem + C::kOffRk);
-  const int q0 = qt * kTile;
   const int h_idx = bh % p.heads, b_idx = bh / p.heads;  // tensor-map coordinates of this (batch, head)
-  bool q_issued = false;
-  if (!(p.inject & 1)) {
-    mbar_arrive_expect_tx(&bars->q_full, C::kNQ * C::kTileBytes);
-#pragma unroll
-    for (int b = 0; b < C::kBoxes; ++b) {
-      tma_load_4d(smem + b * C::kBoxBytes, &p.tm_q1, &bars->q_full, b * 64, q0, h_idx, b_idx);
-      if constexpr (DIFF)
-        tma_load_4d(smem + C::kTileBytes + b * C::kBoxBytes, &p.tm_q2, &bars->q_full, b * 64, q0, h_idx, b_idx);
-    }
-    q_issued = true;
-  }
+  const bool q_issued = !(p.inject & 1);
 
-  int ridx = 0;    // tiles issued into the ring
-  int rk_n = 0;    // rk ring entries issued
+  int ridx = DIFF ? 2 : 1;    // tiles issued into the ring (key tile 0 by issue_first_loads)
+  int rk_n = NORM ? 1 : 0;    // rk ring entries issued
   bool ok = true;
   auto load_tile = [&](const CUtensorMap* map, int j) {
     if (!ok) return;
@@ -183,7 +215,7 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
 
   if constexpr (!DIFF) {
     // consumption order: K0, K1, K2, then per j: V_j, K_{j+3}
-    for (int j = 0; j < 3 && j < n_kt; ++j) {
+    for (int j = 1; j < 3 && j < n_kt; ++j) {
       load_rk(j);
       load_tile(&p.tm_k1, j);
     }
@@ -196,9 +228,6 @@ __device__ void run_producer(const TcFwdParams& p, uint8_t* smem, Bars* bars, co
     }
   } else {
     // consumption order: K1_0, K2_0, K1_1, then per j: K2_{j+1}, V_j, K1_{j+2}
-    load_rk(0);
-    load_tile(&p.tm_k1, 0);
-    load_tile(&p.tm_k2, 0);
     if (n_kt > 1) {
       load_rk(1);
       load_tile(&p.tm_k1, 1);
@@ -495,38 +524,55 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     }
   }
 
-  // epilogue: O (f32 in TMEM) -> global, D / kTransformWG columns per warpgroup
+  // epilogue: O (f32 in TMEM) -> bf16 (or f32) rows staged in the K/V ring,
+  // idle once every product has completed, in the 128-B swizzled layout of
+  // the output tensor map; then one TMA store per 128-byte column box.  The
+  // stores are coalesced (one thread per row would write 32 rows per warp
+  // instruction) and TMA clips rows past S.  Every transform thread reaches
+  // the barrier, also one whose wait gave up.
   if (ok) ok = mbar_wait_warp(&bars->o_full, 0, ctl, ST_TR_O);
-  if (!ok) return;
-  tc_fence_after();
-  constexpr int kCols = D / kTransformWG;
-  static_assert(kCols % 32 == 0, "epilogue reads 32-column chunks");
-  const bool row_ok = grow < p.S;
-  const size_t row_off = (static_cast<size_t>(bh) * p.S + (row_ok ? grow : 0)) * D;
+  uint8_t* stage = smem + C::kOffRing;
+  if (ok) {
+    tc_fence_after();
+    constexpr int kCols = D / kTransformWG;
+    static_assert(kCols % 32 == 0, "epilogue reads 32-column chunks");
+    uint8_t* srow = stage + row * 128;
+    const uint32_t sw = static_cast<uint32_t>(row & 7);
 #pragma unroll
-  for (int c0 = 0; c0 < kCols; c0 += 32) {
-    const int col = wg * kCols + c0;
-    uint32_t o[32];
-    tmem_ld32(tmem + lane_off + C::kColO + col, o);
-    tmem_wait_ld();
-    if (!row_ok) continue;
-    if (p.out_f32) {
-      float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row_off + col);
+    for (int c0 = 0; c0 < kCols; c0 += 32) {
+      const int col = wg * kCols + c0;
+      uint32_t o[32];
+      tmem_ld32(tmem + lane_off + C::kColO + col, o);
+      tmem_wait_ld();
+      if (p.out_f32) {
 #pragma unroll
-      for (int t = 0; t < 8; ++t)
-        dst[t] = make_float4(__uint_as_float(o[4 * t]), __uint_as_float(o[4 * t + 1]), __uint_as_float(o[4 * t + 2]),
-                             __uint_as_float(o[4 * t + 3]));
-    } else {
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row_off + col);
+        for (int t = 0; t < 8; ++t) {
+          const int c = col + 4 * t;  // box c / 32, 16-B chunk (c % 32) / 4
+          *reinterpret_cast<uint4*>(srow + (c >> 5) * C::kBoxBytes + ((((c & 31) >> 2) ^ sw) << 4)) =
+              make_uint4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
+        }
+      } else {
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        uint32_t w[4];
+        for (int t = 0; t < 4; ++t) {
+          const int c = col + 8 * t;  // box c / 64, 16-B chunk (c % 64) / 8
+          uint32_t w[4];
 #pragma unroll
-        for (int h = 0; h < 4; ++h)
-          w[h] = pack_bf16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]));
-        dst[t] = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int h = 0; h < 4; ++h)
+            w[h] = pack_bf16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]));
+          *reinterpret_cast<uint4*>(srow + (c >> 6) * C::kBoxBytes + ((((c & 63) >> 3) ^ sw) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
       }
     }
+    fence_proxy_async_smem();
+  }
+  ok = named_barrier_and(2, 32 * kTransformWarps, ok);
+  if (ok && warp == 2 && lane == 0) {
+    const int n_boxes = p.out_f32 ? D / 32 : D / 64;
+    const int box_cols = p.out_f32 ? 32 : 64;
+    for (int b = 0; b < n_boxes; ++b) tma_store_3d(&p.tm_out, stage + b * C::kBoxBytes, b * box_cols, q0, bh);
+    bulk_commit_group();
+    bulk_wait_group_read0();  // the shared-memory source stays valid until read
   }
 }
 
@@ -575,15 +621,8 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
     }
     bars->abort_flag = 0;
     fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tm_q1);
-    tma_prefetch_desc(&p.tm_k1);
+    issue_first_loads<D, DIFF, NORM>(p, smem, bars, bh, qt);
     tma_prefetch_desc(&p.tm_v);
-    if constexpr (DIFF) {
-      tma_prefetch_desc(&p.tm_q2);
-      tma_prefetch_desc(&p.tm_k2);
-    }
   }
   if (warp == 1) {
     tmem_alloc(&bars->tmem_base, 512);
