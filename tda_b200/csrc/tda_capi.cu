@@ -66,9 +66,10 @@ int make_map(CUtensorMap* m, const void* base, int64_t BH, int64_t S, int64_t D)
   return TDA_OK;
 }
 
-// The forward output, contiguous (BH, S, D) bf16 or f32, as 3-D {D, S, BH};
-// box {128 bytes of elements, 128 rows, 1}, 128-B swizzle (the layout the
-// epilogue stages each 128-row tile in before its TMA store).
+// A contiguous (BH, S, D) bf16 or f32 output array (forward output, fp32
+// gradients) as 3-D {D, S, BH}; box {128 bytes of elements, 128 rows, 1},
+// 128-B swizzle (the layout the epilogues stage each 128-row tile in before
+// its TMA store).
 int make_out_map(CUtensorMap* m, void* out, bool f32, int64_t BH, int64_t S, int64_t D) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
@@ -427,6 +428,9 @@ int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, 
     if ((e = make_map(&prm.tm_k, k, batch_heads, seq_len, head_dim))) return e;
     if ((e = make_map(&prm.tm_v, v, batch_heads, seq_len, head_dim))) return e;
     if ((e = make_map(&prm.tm_do, dout, batch_heads, seq_len, head_dim))) return e;
+    if ((e = make_out_map(&prm.tm_dq, dq, true, batch_heads, seq_len, head_dim))) return e;
+    if ((e = make_out_map(&prm.tm_dk, dk, true, batch_heads, seq_len, head_dim))) return e;
+    if ((e = make_out_map(&prm.tm_dv, dv, true, batch_heads, seq_len, head_dim))) return e;
     cudaError_t ce;
     if (normalize && (ce = tda::launch_key_norms(k, 1, rk, BH, S, S_pad, D, st)) != cudaSuccess)
       return cuda_fail(ce, "key table launch");

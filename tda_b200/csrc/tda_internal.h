@@ -111,6 +111,9 @@ struct TcBwdParams {
   CUtensorMap tm_k;
   CUtensorMap tm_v;
   CUtensorMap tm_do;
+  CUtensorMap tm_dq;  // fp32 gradients, contiguous (BH, S, D) as 3-D {D, S, BH}: box {32, 128, 1}, 128-B swizzle
+  CUtensorMap tm_dk;
+  CUtensorMap tm_dv;
   const float* rk;   // key table of k
   const float2* qc;  // query table
   float* dq;

@@ -110,6 +110,7 @@ struct DqCfg : BCfg<D> {
   static constexpr int kSlotsRaw = (kSmemBudget - kFixed) / B::kTileBytes;
   static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
   static_assert(kSlots >= 3, "not enough shared memory for the K/V ring");
+  static_assert(kSlots * B::kTileBytes >= kTile * D * 4, "the ring must hold the fp32 dQ tile");
   static constexpr int kOffRing = 2 * B::kTileBytes;
   static constexpr int kOffRk = kOffRing + kSlots * B::kTileBytes;
   static constexpr int kOffBar = kOffRk + kRkFloats * 4;
@@ -436,46 +437,59 @@ __device__ void dq_transform(const TcBwdParams& p, uint8_t* smem, DqBars* bars, 
       if constexpr (NORM) mbar_arrive(&bars->rk_empty[re]);
     }
   }
-  // epilogue: dq = rq (dqh - (dqh . qh) qh) with qh = q rq (NORM), else dqh
+  // epilogue: dq = rq (dqh - (dqh . qh) qh) with qh = q rq (NORM), else dqh.
+  // fp32 rows are staged in the idle K/V ring (128-B swizzled 32-column
+  // boxes) and written by TMA stores: coalesced, rows past S clipped.  Every
+  // transform thread reaches the barrier, also one whose wait gave up.
   if (ok) ok = mbar_wait_warp(&bars->o_full, 0, ctl, ST_BQ_TR);
-  if (!ok) return;
-  tc_fence_after();
-  float dot = 0.f;
-  if constexpr (NORM) {
+  uint8_t* stage = smem + C::kOffRing;
+  if (ok) {
+    tc_fence_after();
+    float dot = 0.f;
+    if constexpr (NORM) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        float x[32];
+        tmem_ld32(tmem + lane_off + C::kColO + c0, o);
+        load_row32(smem, row, c0, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) dot = fmaf(__uint_as_float(o[t]), x[t], dot);
+      }
+      dot *= rq;  // dqh . qh
+    }
+    const bool big = rq < 1e12f;
+    uint8_t* srow = stage + row * 128;
+    const uint32_t sw = static_cast<uint32_t>(row & 7);
+#pragma unroll 1
+    for (int c0 = wg * (D / 2); c0 < (wg + 1) * (D / 2); c0 += 32) {
       uint32_t o[32];
       float x[32];
       tmem_ld32(tmem + lane_off + C::kColO + c0, o);
-      load_row32(smem, row, c0, x);
+      if constexpr (NORM) load_row32(smem, row, c0, x);
       tmem_wait_ld();
 #pragma unroll
-      for (int t = 0; t < 32; ++t) dot = fmaf(__uint_as_float(o[t]), x[t], dot);
-    }
-    dot *= rq;  // dqh . qh
-  }
-  const bool big = rq < 1e12f;
-  const bool row_ok = grow < p.S;
-  float* dst = p.dq + (static_cast<size_t>(bh) * p.S + (row_ok ? grow : 0)) * D;
-#pragma unroll 1
-  for (int c0 = wg * (D / 2); c0 < (wg + 1) * (D / 2); c0 += 32) {
-    uint32_t o[32];
-    float x[32];
-    tmem_ld32(tmem + lane_off + C::kColO + c0, o);
-    if constexpr (NORM) load_row32(smem, row, c0, x);
-    tmem_wait_ld();
-    if (!row_ok) continue;
+      for (int t = 0; t < 32; t += 4) {
+        float v[4];
 #pragma unroll
-    for (int t = 0; t < 32; t += 4) {
-      float v[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float g = __uint_as_float(o[t + e]);
-        if constexpr (NORM) g = rq * (big ? g - dot * x[t + e] * rq : g);
-        v[e] = g;
+        for (int e = 0; e < 4; ++e) {
+          float g = __uint_as_float(o[t + e]);
+          if constexpr (NORM) g = rq * (big ? g - dot * x[t + e] * rq : g);
+          v[e] = g;
+        }
+        const int c = c0 + t;  // box c / 32, 16-B chunk (c % 32) / 4
+        *reinterpret_cast<float4*>(srow + (c >> 5) * C::kBoxBytes + ((((c & 31) >> 2) ^ sw) << 4)) =
+            make_float4(v[0], v[1], v[2], v[3]);
       }
-      *reinterpret_cast<float4*>(dst + c0 + t) = make_float4(v[0], v[1], v[2], v[3]);
     }
+    fence_proxy_async_smem();
+  }
+  ok = named_barrier_and(2, 32 * kTrWarps, ok);
+  if (ok && warp == 2 && lane == 0) {
+    for (int b = 0; b < D / 32; ++b) tma_store_3d(&p.tm_dq, stage + b * C::kBoxBytes, b * 32, qt * kTile, bh);
+    bulk_commit_group();
+    bulk_wait_group_read0();  // the shared-memory source stays valid until read
   }
 }
 
@@ -551,6 +565,7 @@ struct DkvCfg : BCfg<D> {
   static constexpr int kSlotsRaw = (kSmemBudget - kFixed) / B::kTileBytes;
   static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
   static_assert(kSlots >= 2, "not enough shared memory for the Q/dout ring");
+  static_assert(kSlots * B::kTileBytes >= 2 * kTile * D * 4, "the ring must hold the fp32 dK and dV tiles");
   static constexpr int kOffRing = 2 * B::kTileBytes;
   static constexpr int kOffQc = kOffRing + kSlots * B::kTileBytes;
   static constexpr int kOffBar = kOffQc + kQcFloats * 4;
@@ -758,58 +773,67 @@ __device__ void dkv_transform(const TcBwdParams& p, uint8_t* smem, DkvBars* bars
       mbar_arrive(&bars->qc_empty[e]);
     }
   }
+  // epilogue: dV and dkh -> dk = rk (dkh - (dkh . kh) kh) (NORM), fp32 rows
+  // staged in the idle Q/dout ring (dK boxes, then dV boxes) and written by
+  // TMA; with accumulate_dv the dV tile is added into global memory by a TMA
+  // reduce-add.  Every transform thread reaches the barrier.
   if (ok) ok = mbar_wait_warp(&bars->o_full, 0, ctl, ST_BK_TR);
-  if (!ok) return;
-  tc_fence_after();
-  const bool row_ok = gkey < p.S;
-  const size_t off = (static_cast<size_t>(bh) * p.S + (row_ok ? gkey : 0)) * D;
-  float dot = 0.f;
-  if constexpr (NORM) {
+  uint8_t* stage_k = smem + C::kOffRing;
+  uint8_t* stage_v = stage_k + (D / 32) * C::kBoxBytes;
+  if (ok) {
+    tc_fence_after();
+    float dot = 0.f;
+    if constexpr (NORM) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t o[32];
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        float x[32];
+        tmem_ld32(tmem + lane_off + C::kColDK + c0, o);
+        load_row32(smem, row, c0, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) dot = fmaf(__uint_as_float(o[t]), x[t], dot);
+      }
+      dot *= rk;  // dkh . kh
+    }
+    const bool big = rk < 1e12f;
+    const uint32_t sw = static_cast<uint32_t>(row & 7);
+#pragma unroll 1
+    for (int c0 = wg * (D / 2); c0 < (wg + 1) * (D / 2); c0 += 32) {
+      uint32_t ok_[32], ov[32];
       float x[32];
-      tmem_ld32(tmem + lane_off + C::kColDK + c0, o);
-      load_row32(smem, row, c0, x);
+      tmem_ld32(tmem + lane_off + C::kColDK + c0, ok_);
+      tmem_ld32(tmem + lane_off + C::kColDV + c0, ov);
+      if constexpr (NORM) load_row32(smem, row, c0, x);
       tmem_wait_ld();
 #pragma unroll
-      for (int t = 0; t < 32; ++t) dot = fmaf(__uint_as_float(o[t]), x[t], dot);
+      for (int t = 0; t < 32; t += 4) {
+        float kv[4];
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          float g = __uint_as_float(ok_[t + e2]);
+          if constexpr (NORM) g = rk * (big ? g - dot * x[t + e2] * rk : g);
+          kv[e2] = g;
+        }
+        const int c = c0 + t;  // box c / 32, 16-B chunk (c % 32) / 4
+        const uint32_t off = row * 128 + (c >> 5) * C::kBoxBytes + ((((c & 31) >> 2) ^ sw) << 4);
+        *reinterpret_cast<float4*>(stage_k + off) = make_float4(kv[0], kv[1], kv[2], kv[3]);
+        *reinterpret_cast<uint4*>(stage_v + off) = make_uint4(ov[t], ov[t + 1], ov[t + 2], ov[t + 3]);
+      }
     }
-    dot *= rk;  // dkh . kh
+    fence_proxy_async_smem();
   }
-  const bool big = rk < 1e12f;
-#pragma unroll 1
-  for (int c0 = wg * (D / 2); c0 < (wg + 1) * (D / 2); c0 += 32) {
-    uint32_t ok_[32], ov[32];
-    float x[32];
-    tmem_ld32(tmem + lane_off + C::kColDK + c0, ok_);
-    tmem_ld32(tmem + lane_off + C::kColDV + c0, ov);
-    if constexpr (NORM) load_row32(smem, row, c0, x);
-    tmem_wait_ld();
-    if (!row_ok) continue;
-    float* dk = p.dk + off + c0;
-    float* dv = p.dv + off + c0;
-#pragma unroll
-    for (int t = 0; t < 32; t += 4) {
-      float kv[4], vv[4];
-#pragma unroll
-      for (int e2 = 0; e2 < 4; ++e2) {
-        float g = __uint_as_float(ok_[t + e2]);
-        if constexpr (NORM) g = rk * (big ? g - dot * x[t + e2] * rk : g);
-        kv[e2] = g;
-        vv[e2] = __uint_as_float(ov[t + e2]);
-      }
-      *reinterpret_cast<float4*>(dk + t) = make_float4(kv[0], kv[1], kv[2], kv[3]);
-      float4 dvv = make_float4(vv[0], vv[1], vv[2], vv[3]);
-      if (p.accumulate_dv) {
-        const float4 old = *reinterpret_cast<const float4*>(dv + t);
-        dvv.x += old.x;
-        dvv.y += old.y;
-        dvv.z += old.z;
-        dvv.w += old.w;
-      }
-      *reinterpret_cast<float4*>(dv + t) = dvv;
+  ok = named_barrier_and(2, 32 * kTrWarps, ok);
+  if (ok && warp == 2 && lane == 0) {
+    for (int b = 0; b < D / 32; ++b) {
+      tma_store_3d(&p.tm_dk, stage_k + b * C::kBoxBytes, b * 32, kt * kTile, bh);
+      if (p.accumulate_dv)
+        tma_reduce_add_3d(&p.tm_dv, stage_v + b * C::kBoxBytes, b * 32, kt * kTile, bh);
+      else
+        tma_store_3d(&p.tm_dv, stage_v + b * C::kBoxBytes, b * 32, kt * kTile, bh);
     }
+    bulk_commit_group();
+    bulk_wait_group_read0();  // the shared-memory sources stay valid until read
   }
 }
 
