@@ -449,7 +449,9 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
           const uint8_t* rb = smem + t * C::kTileBytes + bx * C::kBoxBytes + row * 128;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int cc = 4 * wg + ((k + row) & 3);  // rotated start: fewer bank conflicts
+            // logical chunk cc sits at (cc ^ (row & 7)): for one cc the 8 rows of
+            // each group of 8 lanes hit 8 different 16-B bank groups
+            const int cc = 4 * wg + k;
             const uint4 u = *reinterpret_cast<const uint4*>(rb + ((cc ^ (row & 7)) << 4));
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
