@@ -56,6 +56,7 @@ struct TcFwdParams {
   float tau_scale;    // 2 / D
   unsigned long long timeout_ns;
   int inject;         // test hook: bit 0 = producer never loads Q (forces a timeout)
+  unsigned* item_ctr;  // persistent kernel: zeroed work-item counter (null: one CTA per query tile)
 };
 
 cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,

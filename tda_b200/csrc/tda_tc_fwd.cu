@@ -34,7 +34,9 @@
 // in the status word, drains its in-flight copies / MMAs, frees TMEM and exits.
 #include <cuda_bf16.h>
 
+#include <atomic>
 #include <cstdio>
+#include <cstdlib>
 
 #include "tda_internal.h"
 #include "tda_ptx.cuh"
@@ -261,17 +263,18 @@ __device__ __forceinline__ int ring_k1(int m) { return m == 0 ? 0 : (m == 1 ? 2 
 __device__ __forceinline__ int ring_k2(int m) { return m == 0 ? 1 : 3 * m; }
 __device__ __forceinline__ int ring_v(int j, int n_kt) { return j <= n_kt - 2 ? 4 + 3 * j : 3 * n_kt - 1; }
 
-template <int D, bool DIFF>
+// C: shared-memory layout (ring, box and tile sizes, TMEM columns); B: the
+// barrier block (slot_full / slot_empty / tile_mask) of the kernel using it.
+template <int D, bool DIFF, class C = Cfg<D, DIFF>, class B = Bars>
 struct MmaIssuer {
-  using C = Cfg<D, DIFF>;
-  Bars* bars;
+  B* bars;
   const WaitCtl& ctl;
   uint32_t tmem;
   uint32_t ring_base;
   bool ok;
   bool o_started;
 
-  __device__ MmaIssuer(uint8_t* smem, Bars* b, const WaitCtl& c, uint32_t t)
+  __device__ MmaIssuer(uint8_t* smem, B* b, const WaitCtl& c, uint32_t t)
       : bars(b), ctl(c), tmem(t), ring_base(smem_u32(smem + C::kOffRing)), ok(true), o_started(false) {}
 
   // wait for ring entry `idx` to land; returns its slot
@@ -657,8 +660,679 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
   }
 }
 
+// ================================================================ persistent
+// One CTA per SM; each CTA takes work items -- one 128-row query tile of one
+// (batch, head) -- from a global counter, in the same grouped longest-first
+// order as the one-tile-per-CTA launch, so the items in flight still cover a
+// few (batch, head) slices and late items are the short ones.  Every ring,
+// S slot and barrier phase continues across items (global tile and ring
+// counters), so the K/V ring does not drain between items and one item's
+// start-up overlaps the previous one's last products:
+//   rect: two query buffers; the next item's Q is loaded after the current
+//         item's last K/V load, and a finished item's query buffer stages its
+//         output for the TMA store.
+//   diff: one Q1/Q2 buffer, reloaded as soon as the current item's last QK
+//         products have completed; the output is written directly.
+template <int D, bool DIFF>
+struct PCfg {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kBoxBytes = kTile * 128;
+  static constexpr int kTileBytes = kTile * D * 2;
+  static constexpr int kNQ = DIFF ? 2 : 1;
+  static constexpr int kQBufs = DIFF ? 1 : 2;
+  static constexpr int kQBytes = kNQ * kTileBytes;  // one item's query tile(s)
+  static constexpr int kRkPerTile = (DIFF ? 2 : 1) * (kTile + 8);
+  static constexpr int kRkFloats = kRkRing * kRkPerTile;
+  static constexpr int kBarBytes = 1024;
+  // norm partial sums, one set per item parity: a set is rewritten two items
+  // later, after a barrier that follows every read of it
+  static constexpr int kQssFloats = kNQ * kTransformWG * kTile;
+  static constexpr int kQssBytes = 2 * kQssFloats * 4;
+  static constexpr int kFixed = kQBufs * kQBytes + kRkFloats * 4 + kBarBytes + kQssBytes + 1024;
+  static constexpr int kSlotsRaw = (kSmemBudget - kFixed) / kTileBytes;
+  static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
+  static_assert(kSlots >= 3, "not enough shared memory for the K/V ring");
+  static constexpr int kOffRing = kQBufs * kQBytes;
+  static constexpr int kOffRk = kOffRing + kSlots * kTileBytes;
+  static constexpr int kOffBar = kOffRk + kRkFloats * 4;
+  static constexpr int kOffQss = kOffBar + kBarBytes;
+  static constexpr int kSmemBytes = kOffQss + kQssBytes + 1024;
+  static constexpr int kSSlots = DIFF ? 2 : 3;
+  static constexpr int kColS2 = 128;
+  static constexpr int kColO = 384;
+  static __device__ __forceinline__ uint32_t col_s(int slot) {
+    return DIFF ? (slot ? 256u : 0u) : static_cast<uint32_t>(slot * 128);
+  }
+  static constexpr uint32_t kIdescQK = idesc_f16(128, 128, true, false);
+  static constexpr uint32_t kIdescPV = idesc_f16(128, D, true, true);
+  // ring entries per key tile: K and V (rect); K1, K2, V (diff)
+  static constexpr int kLoadsPerTile = DIFF ? 3 : 2;
+};
+
+struct PBars {
+  uint64_t q_full[2];
+  uint64_t q_empty[2];   // rect: last QK committed + output stored; diff: both issuers' last QK + norms read
+  uint64_t o_full;
+  uint64_t o_empty;      // every transform warp holds O in registers
+  uint64_t drain;
+  uint64_t drain2;
+  uint64_t s_full[3];
+  uint64_t p_full[3];
+  uint64_t s2_free[2];
+  uint64_t rk_full[kRkRing];
+  uint64_t rk_empty[kRkRing];
+  uint64_t slot_full[8];
+  uint64_t slot_empty[8];
+  uint64_t item_full[2];
+  uint64_t item_empty[2];
+  int item[2];           // work item index, -1 = no more work
+  uint32_t tmem_base;
+  int abort_flag;
+  uint32_t tile_mask[3]; // tag = global tile index + 1
+};
+static_assert(sizeof(PBars) <= 1024, "barrier block too large");
+
+constexpr int ST_PROD_Q = 0x103, ST_PROD_ITEM = 0x104, ST_MMA_ITEM = 0x205, ST_MMA_O = 0x206, ST_TR_ITEM = 0x305;
+
+__device__ __forceinline__ void decode_item(const TcFwdParams& p, int idx, int& bh, int& qt) {
+  const int per_group = kHeadGroup * p.n_qtiles;
+  const int g0 = (idx / per_group) * kHeadGroup;
+  const int gsz = min(kHeadGroup, p.BH - g0);
+  const int r = idx % per_group;
+  bh = g0 + r % gsz;
+  qt = p.n_qtiles - 1 - r / gsz;
+}
+
+template <int D, bool DIFF, bool NORM>
+__device__ void p_producer(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, int n_items) {
+  using C = PCfg<D, DIFF>;
+  uint8_t* ring = smem + C::kOffRing;
+  float* rk_s = reinterpret_cast<float*>(smem + C::kOffRk);
+  int ridx = 0;  // ring entries issued (all items)
+  int rk_n = 0;  // key-table ring entries issued (= key tiles of all items)
+  int q_n = 0;   // query loads issued
+  bool ok = true;
+  int h_idx = 0, b_idx = 0, bh = 0;
+  auto load_tile = [&](const CUtensorMap* map, int j) {
+    if (!ok) return;
+    const int slot = ridx % C::kSlots;
+    if (!mbar_wait(&bars->slot_empty[slot], ((ridx / C::kSlots) & 1) ^ 1, ctl, ST_PROD_SLOT)) {
+      ok = false;
+      return;
+    }
+    mbar_arrive_expect_tx(&bars->slot_full[slot], C::kTileBytes);
+    uint8_t* dst = ring + slot * C::kTileBytes;
+#pragma unroll
+    for (int b = 0; b < C::kBoxes; ++b)
+      tma_load_4d(dst + b * C::kBoxBytes, map, &bars->slot_full[slot], b * 64, j * kTile, h_idx, b_idx);
+    ++ridx;
+  };
+  auto load_rk = [&](int j) {
+    if constexpr (NORM) {
+      if (!ok) return;
+      const int e = rk_n % kRkRing;
+      if (!mbar_wait(&bars->rk_empty[e], ((rk_n / kRkRing) & 1) ^ 1, ctl, ST_PROD_RK)) {
+        ok = false;
+        return;
+      }
+      mbar_arrive_expect_tx(&bars->rk_full[e], C::kRkPerTile * 4);
+      float* dst = rk_s + e * C::kRkPerTile;
+      constexpr int kNB = DIFF ? 2 : 1;
+      const size_t off = static_cast<size_t>(bh) * p.S_pad + static_cast<size_t>(j) * kTile;
+      const size_t moff = static_cast<size_t>(p.BH) * p.S_pad + static_cast<size_t>(bh) * (p.S_pad / 16) +
+                          static_cast<size_t>(j) * (kTile / 16);
+      bulk_load(dst, p.rk1 + off, kTile * 4, &bars->rk_full[e]);
+      if constexpr (DIFF) bulk_load(dst + kTile, p.rk2 + off, kTile * 4, &bars->rk_full[e]);
+      bulk_load(dst + kNB * kTile, p.rk1 + moff, 32, &bars->rk_full[e]);
+      if constexpr (DIFF) bulk_load(dst + kNB * kTile + 8, p.rk2 + moff, 32, &bars->rk_full[e]);
+    }
+    ++rk_n;
+  };
+  // publish item `it` (index or -1) to the consumers
+  auto publish = [&](int it, int idx) {
+    if (!ok) return;
+    const int e = it & 1;
+    if (!mbar_wait(&bars->item_empty[e], ((it >> 1) & 1) ^ 1, ctl, ST_PROD_ITEM)) {
+      ok = false;
+      return;
+    }
+    bars->item[e] = idx;
+    mbar_arrive(&bars->item_full[e]);
+  };
+  // query tile(s) of item `it` into its buffer, once the buffer's previous
+  // item has released it
+  auto load_q = [&](int it, int qbh, int qt) {
+    if (!ok) return;
+    const int b = DIFF ? 0 : (it & 1);
+    const int use = DIFF ? it : (it >> 1);
+    if (use > 0 && !mbar_wait(&bars->q_empty[b], (use - 1) & 1, ctl, ST_PROD_Q)) {
+      ok = false;
+      return;
+    }
+    if (p.inject & 1) return;
+    const int qh = qbh % p.heads, qb = qbh / p.heads;
+    uint8_t* dst = smem + b * C::kQBytes;
+    mbar_arrive_expect_tx(&bars->q_full[b], C::kQBytes);
+#pragma unroll
+    for (int x = 0; x < C::kBoxes; ++x) {
+      tma_load_4d(dst + x * C::kBoxBytes, &p.tm_q1, &bars->q_full[b], x * 64, qt * kTile, qh, qb);
+      if constexpr (DIFF)
+        tma_load_4d(dst + C::kTileBytes + x * C::kBoxBytes, &p.tm_q2, &bars->q_full[b], x * 64, qt * kTile, qh, qb);
+    }
+    ++q_n;
+  };
+  auto fetch = [&]() {
+    const int idx = static_cast<int>(atomicAdd(p.item_ctr, 1u));
+    return idx < n_items ? idx : -1;
+  };
+
+  int it = 0;
+  int cur = fetch();
+  publish(0, cur);
+  if (cur >= 0) {
+    int qt0;
+    decode_item(p, cur, bh, qt0);
+    load_q(0, bh, qt0);
+  }
+  while (cur >= 0 && ok) {
+    int qt;
+    decode_item(p, cur, bh, qt);
+    h_idx = bh % p.heads;
+    b_idx = bh / p.heads;
+    const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
+    if constexpr (!DIFF) {
+      // consumption order: K0, K1, K2, then per j: V_j, K_{j+3}
+      for (int j = 0; j < 3 && j < n_kt; ++j) {
+        load_rk(j);
+        load_tile(&p.tm_k1, j);
+      }
+      for (int j = 0; j < n_kt && ok; ++j) {
+        load_tile(&p.tm_v, j);
+        if (j + 3 < n_kt) {
+          load_rk(j + 3);
+          load_tile(&p.tm_k1, j + 3);
+        }
+      }
+    } else {
+      // consumption order: K1_0, K2_0, K1_1, then per j: K2_{j+1}, V_j, K1_{j+2}
+      load_rk(0);
+      load_tile(&p.tm_k1, 0);
+      load_tile(&p.tm_k2, 0);
+      if (n_kt > 1) {
+        load_rk(1);
+        load_tile(&p.tm_k1, 1);
+      }
+      for (int j = 0; j < n_kt && ok; ++j) {
+        if (j + 1 < n_kt) load_tile(&p.tm_k2, j + 1);
+        load_tile(&p.tm_v, j);
+        if (j + 2 < n_kt) {
+          load_rk(j + 2);
+          load_tile(&p.tm_k1, j + 2);
+        }
+      }
+    }
+    const int nxt = fetch();
+    publish(it + 1, nxt);
+    if (nxt >= 0) {
+      int nbh, nqt;
+      decode_item(p, nxt, nbh, nqt);
+      load_q(it + 1, nbh, nqt);
+    }
+    cur = nxt;
+    ++it;
+  }
+  if (!ok) {
+    // abort: wait for the copies still in flight (newest per ring slot, rk
+    // entry and query buffer)
+    const int first = ridx > C::kSlots ? ridx - C::kSlots : 0;
+    for (int i = first; i < ridx; ++i) drain_wait(&bars->slot_full[i % C::kSlots], (i / C::kSlots) & 1, ctl);
+    if constexpr (NORM) {
+      const int rfirst = rk_n > kRkRing ? rk_n - kRkRing : 0;
+      for (int i = rfirst; i < rk_n; ++i) drain_wait(&bars->rk_full[i % kRkRing], (i / kRkRing) & 1, ctl);
+    }
+    const int qfirst = q_n > C::kQBufs ? q_n - C::kQBufs : 0;
+    for (int i = qfirst; i < q_n; ++i) {
+      const int b = DIFF ? 0 : (i & 1);
+      const int use = DIFF ? i : (i >> 1);
+      drain_wait(&bars->q_full[b], use & 1, ctl);
+    }
+  }
+}
+
+// consumer side of the item ring: every consumer thread / warp reads entry
+// `it` and releases it (one arrival per consumer)
+__device__ __forceinline__ int take_item(PBars* bars, int it, const WaitCtl& ctl, int code, bool& ok, bool warp_wide,
+                                         int lane) {
+  const int e = it & 1;
+  bool got = warp_wide ? mbar_wait_warp(&bars->item_full[e], (it >> 1) & 1, ctl, code)
+                       : mbar_wait(&bars->item_full[e], (it >> 1) & 1, ctl, code);
+  int idx = -1;
+  if (got) idx = *reinterpret_cast<volatile int*>(&bars->item[e]);
+  if (warp_wide) __syncwarp();
+  if (got && lane == 0) mbar_arrive(&bars->item_empty[e]);
+  ok = ok && got;
+  return got ? idx : -1;
+}
+
+template <int D, bool DIFF>
+__device__ void p_mma(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, uint32_t tmem) {
+  using C = PCfg<D, DIFF>;
+  MmaIssuer<D, DIFF, C, PBars> m(smem, bars, ctl, tmem);
+  int g = 0;     // global key-tile counter (S slots, tile tags)
+  int base = 0;  // ring position of the item's first entry
+  bool ok = true;
+  for (int it = 0;; ++it) {
+    const int idx = take_item(bars, it, ctl, ST_MMA_ITEM, ok, false, 0);
+    if (idx < 0 || !ok || !m.ok) break;
+    int bh, qt;
+    decode_item(p, idx, bh, qt);
+    const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
+    const int b = DIFF ? 0 : (it & 1);
+    const int use = DIFF ? it : (it >> 1);
+    m.wait(&bars->q_full[b], use & 1, ST_MMA_Q);
+    const uint32_t q1_base = smem_u32(smem + b * C::kQBytes);
+    m.o_started = false;
+    if constexpr (!DIFF) {
+      int r = base;  // ring order: K0, K1, K2, then per j: V_j, K_{j+3}
+      for (int t = 0; t < C::kSSlots && t < n_kt; ++t) {
+        m.qk(r++, C::col_s((g + t) % C::kSSlots), q1_base);
+        m.commit(&bars->s_full[(g + t) % C::kSSlots]);
+        if (t == n_kt - 1) m.commit(&bars->q_empty[b]);  // the item's last QK
+      }
+      for (int j = 0; j < n_kt && m.ok; ++j) {
+        const int G = g + j, slot = G % C::kSSlots;
+        m.wait(&bars->p_full[slot], (G / C::kSSlots) & 1, ST_MMA_P);
+        if (j == 0 && it > 0) m.wait(&bars->o_empty, (it - 1) & 1, ST_MMA_O);
+        m.pv(r++, C::col_s(slot), m.slab_mask(G));
+        if (j + C::kSSlots < n_kt) {
+          m.qk(r++, C::col_s(slot), q1_base);
+          m.commit(&bars->s_full[slot]);
+          if (j + C::kSSlots == n_kt - 1) m.commit(&bars->q_empty[b]);
+        }
+      }
+    } else {
+      m.qk(base + ring_k1(0), C::col_s(g & 1), q1_base);
+      m.commit(&bars->s_full[g & 1]);
+      if (n_kt == 1) m.commit(&bars->q_empty[0]);
+      if (n_kt > 1) {
+        m.qk(base + ring_k1(1), C::col_s((g + 1) & 1), q1_base);
+        m.commit(&bars->s_full[(g + 1) & 1]);
+        if (n_kt == 2) m.commit(&bars->q_empty[0]);
+      }
+      for (int j = 0; j < n_kt && m.ok; ++j) {
+        const int G = g + j, slot = G & 1;
+        m.wait(&bars->p_full[slot], (G >> 1) & 1, ST_MMA_P);
+        if (j == 0 && it > 0) m.wait(&bars->o_empty, (it - 1) & 1, ST_MMA_O);
+        m.pv(base + ring_v(j, n_kt), C::col_s(slot), m.slab_mask(G));
+        if (j + 2 < n_kt) {
+          m.qk(base + ring_k1(j + 2), C::col_s(slot), q1_base);
+          m.commit(&bars->s_full[slot]);
+          if (j + 2 == n_kt - 1) m.commit(&bars->q_empty[0]);
+        }
+      }
+    }
+    m.commit(&bars->o_full);
+    g += n_kt;
+    base += C::kLoadsPerTile * n_kt;
+  }
+  if (!m.ok || !ok) m.drain(&bars->drain);
+}
+
+template <int D>
+__device__ void p_mma_qk2(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, uint32_t tmem) {
+  using C = PCfg<D, true>;
+  MmaIssuer<D, true, C, PBars> m(smem, bars, ctl, tmem);
+  const uint32_t q2_base = smem_u32(smem) + C::kTileBytes;
+  int g = 0, base = 0;
+  bool ok = true;
+  for (int it = 0;; ++it) {
+    const int idx = take_item(bars, it, ctl, ST_MMA_ITEM, ok, false, 0);
+    if (idx < 0 || !ok || !m.ok) break;
+    int bh, qt;
+    decode_item(p, idx, bh, qt);
+    const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
+    m.wait(&bars->q_full[0], it & 1, ST_MMA_Q);
+    for (int j = 0; j < n_kt && m.ok; ++j) {
+      const int G = g + j;
+      // S2 is single-buffered: tile G - 1 must have been read out of it
+      if (G > 0) m.wait(&bars->s2_free[(G - 1) & 1], ((G - 1) >> 1) & 1, ST_MMA_S2);
+      m.qk(base + ring_k2(j), C::kColS2, q2_base);
+      m.commit(&bars->s_full[G & 1]);
+    }
+    m.commit(&bars->q_empty[0]);  // the item's last QK2
+    g += n_kt;
+    base += C::kLoadsPerTile * n_kt;
+  }
+  if (!m.ok || !ok) m.drain(&bars->drain2);
+}
+
+// Query norms of one item into c (and tau for its rows); every transform
+// thread reaches the barrier.  Returns the AND over the transform threads of
+// (ok and the item is real).
+template <int D, bool DIFF, bool NORM, int PM>
+__device__ bool p_prologue(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, int it, int idx,
+                           int row, int wg, bool ok, RowCoef& c, int& bh, int& qt) {
+  using C = PCfg<D, DIFF>;
+  constexpr bool kFold = PM != POW_GENERAL;
+  bh = 0;
+  qt = 0;
+  if (idx >= 0) decode_item(p, idx, bh, qt);
+  const int grow = qt * kTile + row;
+  const float tau = p.beta * sqrtf((2.0f * logf(static_cast<float>(grow + 1))) / static_cast<float>(D));
+  const float lam2 = (DIFF && kFold) ? p.lam_root : 1.0f;
+  c = RowCoef{tau, 1.0f, tau, lam2};
+  bool live = ok && idx >= 0;
+  if constexpr (NORM) {
+    const int b = DIFF ? 0 : (it & 1);
+    const int use = DIFF ? it : (it >> 1);
+    if (live) live = mbar_wait_warp(&bars->q_full[b], use & 1, ctl, ST_TR_Q);
+    float* qss = reinterpret_cast<float*>(smem + C::kOffQss) + (it & 1) * C::kQssFloats;
+    if (live) {
+#pragma unroll 1
+      for (int t = 0; t < C::kNQ; ++t) {
+        float ss = 0.0f;
+#pragma unroll 1
+        for (int bx = 0; bx < C::kBoxes; ++bx) {
+          const uint8_t* rb = smem + b * C::kQBytes + t * C::kTileBytes + bx * C::kBoxBytes + row * 128;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            // logical chunk cc sits at (cc ^ (row & 7)): conflict-free across 8 rows
+            const int cc = 4 * wg + k;
+            const uint4 u = *reinterpret_cast<const uint4*>(rb + ((cc ^ (row & 7)) << 4));
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const float lo = __uint_as_float(w[h] << 16), hi = __uint_as_float(w[h] & 0xFFFF0000u);
+              ss = fmaf(lo, lo, ss);
+              ss = fmaf(hi, hi, ss);
+            }
+          }
+        }
+        qss[(t * kTransformWG + wg) * kTile + row] = ss;
+      }
+    }
+    live = named_barrier_and(1, 32 * kTransformWarps, live);
+    if (live) {
+      const float m1 = fmaxf(sqrtf(qss[row] + qss[kTile + row]), 1e-12f);
+      c.rq1 = 1.0f / m1;
+      c.tq1 = tau * m1;
+      if constexpr (DIFF) {
+        const float m2 = fmaxf(sqrtf(qss[2 * kTile + row] + qss[3 * kTile + row]), 1e-12f);
+        c.rq2 = lam2 / m2;
+        c.tq2 = tau * m2;
+      }
+    }
+  } else {
+    live = named_barrier_and(1, 32 * kTransformWarps, live);
+  }
+  if constexpr (DIFF) {
+    // the query buffer may be reloaded once both issuers' last QK products of
+    // this item are done and the norms have been read (this arrival)
+    if (live && threadIdx.x == 64) mbar_arrive(&bars->q_empty[0]);
+  }
+  return live;
+}
+
+// Transform warps of the persistent kernel.  Per item: key tile 0, then the
+// previous item's epilogue (its O is complete by then, and the current
+// item's first PV waits only for O to be read out), then the remaining key
+// tiles, then the next item's query norms.  Both named barriers (norms: 1,
+// epilogue: 2) are reached by every transform warp in the same order, and
+// whether to go on is decided from their AND-reductions, so a wait that gave
+// up in one warp cannot leave the others at a barrier.
+template <int D, bool DIFF, bool NORM, bool POS, int PM>
+__device__ void p_transform(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, uint32_t tmem,
+                            int warp, int lane) {
+  using C = PCfg<D, DIFF>;
+  constexpr int kChunks = 4 / kTransformWG;
+  static_assert(kChunks == 2, "transform_tile handles two chunks");
+  const int wg = (warp - 2) >> 2;
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;
+  const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+  const float* rk_s = reinterpret_cast<const float*>(smem + C::kOffRk);
+
+  // key tile j (global index G) of the item whose query tile is qt
+  auto tile = [&](int j, int G, int qt, const RowCoef& c) -> bool {
+    const int re = G % kRkRing;
+    if constexpr (NORM) {
+      if (!mbar_wait_warp(&bars->rk_full[re], (G / kRkRing) & 1, ctl, ST_TR_RK)) return false;
+    }
+    const int slot = G % C::kSSlots;
+    if (!mbar_wait_warp(&bars->s_full[slot], (G / C::kSSlots) & 1, ctl, ST_TR_S)) return false;
+    tc_fence_after();
+    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>>(
+        tmem + lane_off, C::col_s(slot), C::kColS2, wg, rk_s + re * C::kRkPerTile, qt * kTile + row - j * kTile,
+        j >= qt, c, p.relu_power, p.lam, [&] {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->s2_free[G & 1]);
+        });
+    const uint32_t wmask = __reduce_or_sync(0xffffffffu, nz) << (2 * kChunks * wg);
+    if (wmask != 0u && lane == 0) {
+      uint32_t* word = &bars->tile_mask[slot];
+      const uint32_t tag = static_cast<uint32_t>(G + 1) << 8;
+      uint32_t old = *reinterpret_cast<volatile uint32_t*>(word), assumed;
+      do {
+        assumed = old;
+        const uint32_t base = (assumed & ~0xFFu) == tag ? assumed : tag;
+        old = atomicCAS(word, assumed, base | wmask);
+      } while (old != assumed);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&bars->p_full[slot]);
+      if constexpr (NORM) mbar_arrive(&bars->rk_empty[re]);
+    }
+    return true;
+  };
+
+  // epilogue of item e_it, 32 columns at a time: O -> registers -> output
+  // (rect bf16: staged in the item's query buffer, free once its last QK and
+  // its norms are done, then TMA-stored); O is handed back (o_empty) once the
+  // last chunk is in registers.  Returns the AND over the transform warps.
+  auto epilogue = [&](int e_it, int e_bh, int e_qt, bool in_ok) -> bool {
+    const bool eok = in_ok && mbar_wait_warp(&bars->o_full, e_it & 1, ctl, ST_TR_O);
+    constexpr int kCols = D / kTransformWG;
+    const int egrow = e_qt * kTile + row;
+    const bool staged = !DIFF && !p.out_f32;
+    uint8_t* stage = smem + (e_it & 1) * C::kQBytes;
+    if (eok) {
+      tc_fence_after();
+      const size_t row_off = (static_cast<size_t>(e_bh) * p.S + (egrow < p.S ? egrow : 0)) * D;
+#pragma unroll 1
+      for (int c0 = 0; c0 < kCols; c0 += 32) {
+        const int col = wg * kCols + c0;
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_off + C::kColO + col, o);
+        tmem_wait_ld();
+        if (c0 + 32 == kCols) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars->o_empty);
+        }
+        if (staged) {
+          uint8_t* srow = stage + row * 128;
+          const uint32_t sw = static_cast<uint32_t>(row & 7);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int cc = col + 8 * t;  // box cc / 64, 16-B chunk (cc % 64) / 8
+            uint32_t w[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+              w[h] = pack_bf16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]));
+            *reinterpret_cast<uint4*>(srow + (cc >> 6) * C::kBoxBytes + ((((cc & 63) >> 3) ^ sw) << 4)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        } else if (egrow < p.S) {
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row_off + col);
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              dst[t] = make_float4(__uint_as_float(o[4 * t]), __uint_as_float(o[4 * t + 1]),
+                                   __uint_as_float(o[4 * t + 2]), __uint_as_float(o[4 * t + 3]));
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + row_off + col);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              uint32_t w[4];
+#pragma unroll
+              for (int h = 0; h < 4; ++h)
+                w[h] = pack_bf16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]));
+              dst[t] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+        }
+      }
+      if (staged) fence_proxy_async_smem();
+    }
+    const bool sok = named_barrier_and(2, 32 * kTransformWarps, eok);
+    if (!DIFF && warp == 2 && lane == 0) {
+      if (staged && sok) {
+        for (int x = 0; x < C::kBoxes; ++x)
+          tma_store_3d(&p.tm_out, stage + x * C::kBoxBytes, x * 64, e_qt * kTile, e_bh);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+      }
+      mbar_arrive(&bars->q_empty[e_it & 1]);  // the query buffer may be reloaded
+    }
+    return sok;
+  };
+
+  bool ok = true;
+  int g = 0, it = 0;
+  const int idx0 = take_item(bars, 0, ctl, ST_TR_ITEM, ok, true, lane);
+  RowCoef c;
+  int bh, qt;
+  bool live = p_prologue<D, DIFF, NORM, PM>(p, smem, bars, ctl, 0, idx0, row, wg, ok, c, bh, qt);
+  ok = live;
+  bool pending = false;  // the previous item's epilogue is still to be done
+  int p_it = 0, p_bh = 0, p_qt = 0;
+  while (live) {
+    const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
+    if (ok) ok = tile(0, g, qt, c);
+    if (pending) {
+      ok = epilogue(p_it, p_bh, p_qt, ok);  // uniform from here
+      pending = false;
+    }
+    for (int j = 1; j < n_kt && ok; ++j) ok = tile(j, g + j, qt, c);
+    const int nidx = take_item(bars, it + 1, ctl, ST_TR_ITEM, ok, true, lane);
+    RowCoef cn;
+    int nbh, nqt;
+    live = p_prologue<D, DIFF, NORM, PM>(p, smem, bars, ctl, it + 1, nidx, row, wg, ok, cn, nbh, nqt);
+    pending = true;
+    p_it = it;
+    p_bh = bh;
+    p_qt = qt;
+    g += n_kt;
+    ++it;
+    c = cn;
+    bh = nbh;
+    qt = nqt;
+    ok = live;
+  }
+  if (pending) epilogue(p_it, p_bh, p_qt, true);
+}
+
+template <int D, bool DIFF, bool NORM, bool POS, int PM>
+__global__ void __maxnreg__(168) tda_tc_fwd_persistent_kernel(const __grid_constant__ TcFwdParams p) {
+  using C = PCfg<D, DIFF>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PBars* bars = reinterpret_cast<PBars*>(smem + C::kOffBar);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_items = p.BH * p.n_qtiles;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->q_full[i], 1);
+      mbar_init(&bars->q_empty[i], DIFF ? 3 : 2);
+      mbar_init(&bars->item_full[i], 1);
+      mbar_init(&bars->item_empty[i], 1 + (DIFF ? 1 : 0) + kTransformWarps);
+      mbar_init(&bars->s2_free[i], kTransformWarps);
+      bars->item[i] = -1;
+    }
+    mbar_init(&bars->o_full, 1);
+    mbar_init(&bars->o_empty, kTransformWarps);
+    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain2, 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->s_full[i], DIFF ? 2 : 1);
+      mbar_init(&bars->p_full[i], kTransformWarps);
+      bars->tile_mask[i] = 0;
+    }
+    for (int i = 0; i < kRkRing; ++i) {
+      mbar_init(&bars->rk_full[i], 1);
+      mbar_init(&bars->rk_empty[i], kTransformWarps);
+    }
+    for (int i = 0; i < C::kSlots; ++i) {
+      mbar_init(&bars->slot_full[i], 1);
+      mbar_init(&bars->slot_empty[i], 1);
+    }
+    bars->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&p.tm_q1);
+    tma_prefetch_desc(&p.tm_k1);
+    tma_prefetch_desc(&p.tm_v);
+    if constexpr (DIFF) {
+      tma_prefetch_desc(&p.tm_q2);
+      tma_prefetch_desc(&p.tm_k2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const WaitCtl ctl{&bars->abort_flag, p.status, p.timeout_ns};
+  if (warp == 0) {
+    if (lane == 0) p_producer<D, DIFF, NORM>(p, smem, bars, ctl, n_items);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) p_mma<D, DIFF>(p, smem, bars, ctl, tmem);
+    __syncwarp();
+  } else if (warp < kQk2Warp) {
+    p_transform<D, DIFF, NORM, POS, PM>(p, smem, bars, ctl, tmem, warp, lane);
+  } else if constexpr (DIFF) {
+    if (lane == 0) p_mma_qk2<D>(p, smem, bars, ctl, tmem);
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D, bool DIFF, bool NORM, bool POS, int PM>
+cudaError_t launch_persistent(const TcFwdParams& p, cudaStream_t stream) {
+  using C = PCfg<D, DIFF>;
+  auto kern = tda_tc_fwd_persistent_kernel<D, DIFF, NORM, POS, PM>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const long long n_items = static_cast<long long>(p.BH) * p.n_qtiles;
+  const unsigned grid = static_cast<unsigned>(n_items < sms ? n_items : sms);
+  kern<<<grid, threads_for<DIFF>(), C::kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
 template <int D, bool DIFF, bool NORM, bool POS, int PM>
 cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
+  if (p.item_ctr) return launch_persistent<D, DIFF, NORM, POS, PM>(p, stream);
   using C = Cfg<D, DIFF>;
   auto kern = tda_tc_fwd_kernel<D, DIFF, NORM, POS, PM>;
   static bool attr_done = false;  // per instantiation; attribute is per-function, idempotent
@@ -712,8 +1386,35 @@ cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, cu
 
 }  // namespace
 
-cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,
+// Work-item counters of the persistent kernel: one per launch in flight, taken
+// round-robin and zeroed in the launch's stream right before it.
+__device__ unsigned g_item_ctr[1024];
+
+static bool persistent_forward_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TDA_B200_FWD_PERSISTENT");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+static cudaError_t prepare_item_counter(TcFwdParams& p, cudaStream_t stream) {
+  static std::atomic<unsigned> next{0};
+  unsigned* base = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&base), g_item_ctr);
+  if (e != cudaSuccess) return e;
+  p.item_ctr = base + (next.fetch_add(1u) % 1024u);
+  return cudaMemsetAsync(p.item_ctr, 0, sizeof(unsigned), stream);
+}
+
+cudaError_t launch_tc_fwd(const TcFwdParams& p_in, int head_dim, bool differential, bool normalize, int pow_mode,
                           cudaStream_t stream) {
+  TcFwdParams p = p_in;
+  p.item_ctr = nullptr;
+  if (persistent_forward_enabled()) {
+    cudaError_t e = prepare_item_counter(p, stream);
+    if (e != cudaSuccess) return e;
+  }
   if (head_dim == 128) return dispatch_diff<128>(p, differential, normalize, pow_mode, stream);
   if (head_dim == 64) return dispatch_diff<64>(p, differential, normalize, pow_mode, stream);
   return cudaErrorInvalidValue;
