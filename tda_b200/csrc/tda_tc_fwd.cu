@@ -1212,12 +1212,16 @@ __device__ void p_transform(const TcFwdParams& p, uint8_t* smem, PBars* bars, co
   int p_it = 0, p_bh = 0, p_qt = 0;
   while (live) {
     const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
-    if (ok) ok = tile(0, g, qt, c);
-    if (pending) {
-      ok = epilogue(p_it, p_bh, p_qt, ok);  // uniform from here
-      pending = false;
+    // one call site of the (large) tile body; iteration 0 is run by every
+    // warp, so the deferred epilogue after it is reached by all of them
+    for (int j = 0; j < n_kt; ++j) {
+      if (ok) ok = tile(j, g + j, qt, c);
+      if (j == 0 && pending) {
+        ok = epilogue(p_it, p_bh, p_qt, ok);  // uniform from here
+        pending = false;
+      }
+      if (!ok) break;
     }
-    for (int j = 1; j < n_kt && ok; ++j) ok = tile(j, g + j, qt, c);
     const int nidx = take_item(bars, it + 1, ctl, ST_TR_ITEM, ok, true, lane);
     RowCoef cn;
     int nbh, nqt;
@@ -1390,12 +1394,20 @@ cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, cu
 // round-robin and zeroed in the launch's stream right before it.
 __device__ unsigned g_item_ctr[1024];
 
-static bool persistent_forward_enabled() {
-  static const bool on = [] {
+// Kernel choice.  Measured on B200 (bf16, beta = 1): the persistent kernel
+// gains where a query tile has few key tiles, so that per-tile start-up and
+// epilogue are a large share -- rect (4,32,4096,128) +4%, (4,32,2048,128)
+// +6.7% -- is even at S = 8192 (rect), loses 4% at head_dim 64
+// ((2,16,2048,64)) and 3.6% on the differential form, whose single Q1/Q2
+// buffer and unstaged output leave its item boundaries on the critical path.
+// TDA_B200_FWD_PERSISTENT=1 / =0 forces either kernel.
+static bool use_persistent_forward(bool differential, int head_dim, int n_qtiles) {
+  static const int forced = [] {
     const char* v = std::getenv("TDA_B200_FWD_PERSISTENT");
-    return v && v[0] == '1';
+    return (v && v[0] == '1') ? 1 : ((v && v[0] == '0') ? 0 : -1);
   }();
-  return on;
+  if (forced >= 0) return forced == 1;
+  return !differential && head_dim == 128 && n_qtiles <= 32;
 }
 
 static cudaError_t prepare_item_counter(TcFwdParams& p, cudaStream_t stream) {
@@ -1411,7 +1423,7 @@ cudaError_t launch_tc_fwd(const TcFwdParams& p_in, int head_dim, bool differenti
                           cudaStream_t stream) {
   TcFwdParams p = p_in;
   p.item_ctr = nullptr;
-  if (persistent_forward_enabled()) {
+  if (use_persistent_forward(differential, head_dim, p.n_qtiles)) {
     cudaError_t e = prepare_item_counter(p, stream);
     if (e != cudaSuccess) return e;
   }
