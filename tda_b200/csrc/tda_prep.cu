@@ -7,8 +7,8 @@
 //   rkmax[bh * S_pad / 16 + g]      = max of rk over keys [16 g, 16 g + 16)
 // (rkmax starts right after rk).  The forward kernels use rkmax to prove a
 // 16-key group of scores lies below the threshold from the raw scores alone.
-// HBM-bound: reads B*H*S*D*2 bytes.  One warp per 16 consecutive keys; 16-byte
-// loads, fp32 sum of squares, IEEE sqrt and divide.
+// HBM-bound: reads B*H*S*D*2 bytes.  One warp per 16 consecutive keys; all of
+// its 16-byte loads issued first, fp32 sums of squares, IEEE sqrt and divide.
 #include <cuda_bf16.h>
 
 #include "tda_internal.h"
@@ -36,21 +36,26 @@ __global__ void __launch_bounds__(256) key_norm_kernel(const __nv_bfloat16* __re
     const int bh = static_cast<int>(g / (S_pad / 16));
     const int j0 = static_cast<int>(g % (S_pad / 16)) * 16;
     const __nv_bfloat16* xb = x + static_cast<long long>(bh / heads) * sb + static_cast<long long>(bh % heads) * sh;
+    // all of the group's 16-byte loads first (more bytes in flight), then
+    // the sums of squares with packed f32x2 FMAs (two accumulators per lane)
+    uint4 u[kIters];
+#pragma unroll
+    for (int it = 0; it < kIters; ++it) {
+      const int j = j0 + it * kRowsPerIter + sub;
+      u[it] = j < S ? reinterpret_cast<const uint4*>(xb + static_cast<long long>(j) * ss_)[sl] : make_uint4(0, 0, 0, 0);
+    }
     float mx = 0.0f;
 #pragma unroll
     for (int it = 0; it < kIters; ++it) {
       const int j = j0 + it * kRowsPerIter + sub;
-      float ss = 0.0f;
-      if (j < S) {
-        const uint4 u = reinterpret_cast<const uint4*>(xb + static_cast<long long>(j) * ss_)[sl];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      const uint32_t w[4] = {u[it].x, u[it].y, u[it].z, u[it].w};
+      float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float lo = __uint_as_float(w[h] << 16), hi = __uint_as_float(w[h] & 0xFFFF0000u);
-          ss = fmaf(lo, lo, ss);
-          ss = fmaf(hi, hi, ss);
-        }
+      for (int h = 0; h < 4; ++h) {
+        const float2 v = make_float2(__uint_as_float(w[h] << 16), __uint_as_float(w[h] & 0xFFFF0000u));
+        acc = __ffma2_rn(v, v, acc);
       }
+      float ss = acc.x + acc.y;
 #pragma unroll
       for (int off = kLanesPerRow / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       const float r = (j < S) ? 1.0f / fmaxf(sqrtf(ss), 1e-12f) : 0.0f;
