@@ -17,7 +17,9 @@ flush is needed between steps).  FLOPs are the dense causal algorithmic count
 3*B*H*S^2*D (QK1, QK2 and one PV), never the executed count.
 
 Prints one JSON line on rank 0.  ``--impl reference`` times the CPU restatement
-of the reference (oracle/) on the host cores instead.
+of the reference (oracle/) on the host cores instead; ``--impl reference-triton``
+times the reference module's own Triton kernel on the GPU (N=1, from
+baseline/_ref, installed by baseline/install_reference.sh).
 """
 from __future__ import annotations
 
@@ -223,6 +225,79 @@ def run_reference(args, rank, world):
         "data": "synthetic", "config": {"workload": describe(name), "sample": sample},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_triton(args, rank, local, world):
+    """--impl reference-triton: the unmodified reference module
+    (``triton_threshold_attention.py``, installed into baseline/_ref by
+    baseline/install_reference.sh) on this GPU, through its public functions,
+    on the same inputs as the tda arm.  The reference upcasts to fp32 and runs
+    its Triton kernel (TF32 dots, the whole S x S score map: ``T.py:66``) once
+    per branch; the normalized rectified form is the reference called on
+    F.normalize(q), F.normalize(k), as each branch of ``T.py:505-512`` does.
+    N = 1 only (the reference has no multi-GPU path)."""
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "reference-triton", "unavailable": "runs at N=1 only"}), flush=True)
+        return 0
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isfile(os.path.join(ref_dir, "triton_threshold_attention.py")):
+        print(json.dumps({"impl": "reference-triton",
+                          "unavailable": "baseline/_ref holds no reference install (baseline/install_reference.sh)"}),
+              flush=True)
+        return 0
+    import torch
+    import torch.nn.functional as F
+    from tda_b200.shard import shard_range
+    sys.path.insert(0, ref_dir)
+    import triton_threshold_attention as ref
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    name = args.config
+    op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
+    xs = make_inputs(name, shard_range(B * H, 1, 0), dev, "bhsd", args.dtype)
+    bt = torch.tensor(beta)
+    if op == "diff":
+        lt = torch.tensor(lam, device=dev)
+
+        def step():
+            return ref.differential_threshold_rela_triton(*xs, bt, lt, p, norm)
+    else:
+        q, k, v = xs
+
+        def step():
+            if norm:
+                return ref.threshold_rela_triton(F.normalize(q, dim=-1), F.normalize(k, dim=-1), v, bt, p)
+            return ref.threshold_rela_triton(q, k, v, bt, p)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(args.steps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        ms.append(a.elapsed_time(b))
+    total = sum(ms)
+    flops = flops_of(op, B * H, S, D)
+    val = flops * args.steps / (total * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": val, "unit": "TFLOP/s", "impl": "reference-triton", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (TF32 dots)",
+        "data": "synthetic",
+        "config": {"workload": describe(name) + (", fp32 inputs" if args.dtype == "f32" else ""),
+                   "how": "reference public API, CUDA events per step on the current stream; FLOPs are the "
+                          "same dense causal algorithmic count as the tda arm",
+                   "flops_per_step": flops},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -604,7 +679,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["tda", "reference"], default="tda")
+    ap.add_argument("--impl", choices=["tda", "reference", "reference-triton"], default="tda",
+                    help="reference: the reference's algorithm on the host cores (the driver's reference arm); "
+                         "reference-triton: the reference module's own Triton kernel on this GPU (N=1)")
     ap.add_argument("--config", choices=sorted(WORKLOADS), default="diff8k")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -620,6 +697,8 @@ def main():
     rank, local, world = env_rank_world()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.impl == "reference-triton":
+        return run_reference_triton(args, rank, local, world)
     if args.backward:
         return run_tda_backward(args, rank, local, world)
     return run_tda(args, rank, local, world)
