@@ -469,7 +469,10 @@ def run_tda(args, rank, local, world):
     # the fp32 path computes the norms inside its kernel; the strided entries
     # run their key-norm pre-pass inside the call (timed with the main kernel)
     separate_norms = norm and not f32 and not strided
-    ws_n = lib.tda_workspace_size(int(op == "diff"), _lib.TDA_BF16, n_bh, S, D, int(norm)) if strided else 0
+    # the strided entries take the key-table workspace; fp32 at head_dim 64 takes
+    # the TF32 split copies of its tensor-core path (other fp32 head dims: none)
+    ws_kind = _lib.TDA_F32 if f32 else _lib.TDA_BF16
+    ws_n = lib.tda_workspace_size(int(op == "diff"), ws_kind, n_bh, S, D, int(norm)) if (strided or f32) else 0
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
     strides = (ctypes.c_int64 * (3 * len(xs)))(*[st for x in xs for st in x.stride()[:3]])
 
@@ -483,10 +486,12 @@ def run_tda(args, rank, local, world):
         if f32:
             if op == "diff":
                 _lib.check(lib.tda_diff_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, n_bh, S, D, beta, lam,
-                                            p, int(norm), None, 0, status.data_ptr(), sp))
+                                            p, int(norm), ws.data_ptr() if ws_n else None, ws_n,
+                                            status.data_ptr(), sp))
             else:
                 _lib.check(lib.tda_rect_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, n_bh, S, D, beta, p,
-                                            int(norm), None, 0, status.data_ptr(), sp))
+                                            int(norm), ws.data_ptr() if ws_n else None, ws_n, status.data_ptr(),
+                                            sp))
         elif strided:
             fn = lib.tda_diff_fwd_strided if op == "diff" else lib.tda_rect_fwd_strided
             extra = (beta, lam, p) if op == "diff" else (beta, p)
@@ -500,7 +505,9 @@ def run_tda(args, rank, local, world):
             _lib.check(lib.tda_rect_fwd_tc(ptr[0], ptr[1], ptr[2], out.data_ptr(), _lib.TDA_BF16, n_bh, S, D, beta,
                                            p, int(norm), rk[0].data_ptr(), status.data_ptr(), sp))
 
-    launches_per_step = (2 if op == "diff" else 1) * int(norm and not f32) + 1
+    n_br = 2 if op == "diff" else 1
+    tf32 = f32 and D == 64  # fp32 on the tensor cores: split pre-pass (2 per branch + V^T) and the forward
+    launches_per_step = (2 * n_br + 2) if tf32 else n_br * int(norm and not f32) + 1
 
     for _ in range(args.warmup):
         launch_norms()
@@ -535,7 +542,11 @@ def run_tda(args, rank, local, world):
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     peak_note = f"bf16_tflops (burst) of {peak_src}"
-    if f32:
+    if tf32:
+        # three TF32 products per fp32 product at the TF32 rate, half the bf16 rate on B200
+        peak = peak / 2.0 / 3.0
+        peak_note = f"bf16_tflops (burst) of {peak_src} / 2 (TF32 rate) / 3 (products per fp32 product)"
+    elif f32:
         # FFMA: 148 SMs x 128 FMA lanes x 2 FLOP x 1.965 GHz (nominal; no measured fp32 figure)
         peak = 148 * 128 * 2 * 1.965e9 / 1e12
         peak_note = "nominal FFMA peak, 148 SMs x 128 lanes x 2 x 1.965 GHz"
@@ -637,7 +648,9 @@ def run_tda(args, rank, local, world):
             "data": "synthetic",
             "pct_bf16_peak": None if f32 else value / world / peak,
             "config": {
-                "workload": describe(name) + (", fp32 inputs (CUDA-core path)" if f32 else "")
+                "workload": describe(name) + ((", fp32 inputs (tensor cores, three TF32 products per product; "
+                                               "main_kernel_ms includes the split pre-pass)") if tf32 else
+                                              (", fp32 inputs (CUDA-core path)" if f32 else ""))
                 + (", (B, S, H, D) storage read in place through the strided entry (main_kernel_ms includes "
                    "its key-norm pre-pass)" if strided else ""),
                 "layout": args.layout,
@@ -650,7 +663,7 @@ def run_tda(args, rank, local, world):
                 "main_kernel_ms_max_rank": main_avg_max,
             },
             "roofline": {
-                "bound": "fp32-fma" if f32 else "tensor",
+                "bound": "tensor" if (tf32 or not f32) else "fp32-fma",
                 "achieved": achieved,
                 "peak": peak,
                 "unit": "TFLOP/s",

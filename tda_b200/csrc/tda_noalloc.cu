@@ -73,9 +73,10 @@ extern "C" int tda_diff_fwd_noalloc(const void* q1, const void* q2, const void* 
                                     void* out, int dtype, int out_dtype, int64_t batch_heads, int64_t seq_len,
                                     int64_t head_dim, float beta, float lambda_param, float relu_power,
                                     int normalize, int* status, void* stream) {
-  const size_t need = tda_workspace_size(1, dtype, batch_heads, seq_len, head_dim, normalize);
+  const size_t need = dtype == TDA_F32 ? 0 : tda_workspace_size(1, dtype, batch_heads, seq_len, head_dim, normalize);
   if (need == 0) {
-    // This configuration uses no scratch at all (fp32 inputs, or no normalize).
+    // This configuration uses no scratch at all (fp32 inputs on the CUDA-core
+    // kernel, or no normalize).
     return tda_diff_fwd(q1, q2, k1, k2, v, out, dtype, out_dtype, batch_heads, seq_len, head_dim, beta,
                         lambda_param, relu_power, normalize, nullptr, 0, status, stream);
   }

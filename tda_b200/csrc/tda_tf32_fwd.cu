@@ -1,0 +1,486 @@
+// Tensor-core forward for fp32 inputs at head_dim 64 (tcgen05, kind::tf32).
+//
+// fp32 results must stay within 1e-5 rel-L2 of an fp64 oracle; one TF32
+// product per score (10-bit mantissa) misses that by far.  Each fp32 operand
+// x is therefore split into h = x rounded to TF32 and l = x - h (exact in
+// fp32) rounded to TF32, and every product is formed from three TF32
+// products, h_a*h_b + h_a*l_b + l_a*h_b.  The dropped l_a*l_b term and l's
+// rounding are ~2^-23 relative and unbiased (both parts rounded to nearest).
+// O += P V uses the same three products, with P split after the threshold /
+// ReLU^p transform.
+// Semantics as the reference forward (triton_threshold_attention.py:19-115,
+// mask-to-zero causal rule, tau(i) = beta*sqrt(2 log(i+1)/D), power branch
+// incl. exp(p*log(x+1e-10))) and its differential wrapper (:489-519: both
+// branches accumulate into one output, the second weighted by -clamp(lambda)).
+//
+// Pre-pass (stream-ordered, into the caller's workspace):
+//   q, k rows -> h, l copies [BH][S][64], and per row 1/m, tau*m (queries) or
+//   1/m (keys), m = max(||x||, 1e-12) when normalized, m = 1 otherwise;
+//   v -> transposed h, l copies [BH][64][S_pad] (zero past S), so that V^T is
+//   a K-major operand like K.
+// Main kernel: one CTA = 128 query rows of one (batch, head); 64-key tiles.
+//   warp 0  TMA producer: Q h/l once per branch, K h/l and V^T h/l rings of
+//           two entries each (K released by QK, V by PV)
+//   warp 1  MMA issuer (one thread): S = Q K^T (3 x 8 MMAs of M128 N64 K8)
+//           into one of two TMEM S slots; P V^T (3 x 8 MMAs, P from TMEM)
+//   warps 2-5  transform: thread = query row = TMEM lane; S -> P, written back
+//           as P_h over S and P_l beside it; adds each tile's P V^T into
+//           fp32 registers; epilogue O -> out.
+// TMEM (64 columns each): S slot b holds the h*h part of S at 128 b (then
+// P_h) and the cross terms at 128 b + 64 (then P_l); the partial O of tile t
+// has its h*h part at 256 + 128 (t % 2) and its cross terms 64 further;
+// the parts are added in fp32 registers, and the tiles' partial O too.
+#include "tda_internal.h"
+#include "tda_ptx.cuh"
+
+namespace tda {
+namespace {
+
+constexpr int kD = 64;
+constexpr int kBM = 128;
+constexpr int kBN = 64;
+constexpr int kThreads = 192;
+constexpr int kBox = 64 * 128;  // one TMA box: 64 rows of 32 fp32 (128 B), 8 KB
+constexpr int kQBytes = 2 * 2 * kBox;  // 128 rows x 64 dims: 2 column boxes x 2 row halves, 32 KB
+constexpr int kKBytes = 2 * kBox;      // 64 keys x 64 dims, 16 KB
+constexpr int kOffQh = 0, kOffQl = kQBytes;
+constexpr int kOffK = 2 * kQBytes;                 // 2 entries x (K_h, K_l)
+constexpr int kOffV = kOffK + 2 * 2 * kKBytes;     // 2 entries x (Vt_h, Vt_l)
+constexpr int kOffBar = kOffV + 2 * 2 * kKBytes;   // 192 KB
+constexpr int kSmemBytes = kOffBar + 256 + 1024;   // + barriers + alignment slack
+constexpr uint32_t kColO = 256;  // two per-tile partial O slots: 256 + 128 e (h*h part, then cross terms)
+constexpr uint32_t kIdesc = (1u << 4)                                  // D f32
+                            | (2u << 7) | (2u << 10)                   // A, B tf32, both K-major
+                            | (static_cast<uint32_t>(64 >> 3) << 17)   // N = 64
+                            | (static_cast<uint32_t>(128 >> 4) << 24);  // M = 128
+
+constexpr int ST_TF_PROD = 0x601, ST_TF_MMA = 0x602, ST_TF_TR = 0x603, ST_TF_DRAIN = 0x604;
+
+struct Tf32Bars {
+  uint64_t q_full, q_empty, drain;
+  uint64_t o_full[2], o_free[2];  // per-tile partial O: written by PV, read by the transform
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], p_full[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Tf32Bars) <= 256, "barrier block too large");
+
+__device__ __forceinline__ uint32_t col_s(int e) { return 128u * static_cast<uint32_t>(e); }
+__device__ __forceinline__ uint32_t col_pl(int e) { return 128u * static_cast<uint32_t>(e) + 64u; }
+
+__device__ __forceinline__ void mma_ss_tf32(uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_tf32(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Waits with a time limit; used only while tearing down after an abort.
+__device__ void tf_drain_wait(uint64_t* bar, uint32_t parity, const WaitCtl& ctl) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(a, parity)) {
+    if (global_timer_ns() - t0 > ctl.timeout_ns) {
+      atomicCAS(ctl.status, 0, ST_TF_DRAIN);
+      return;
+    }
+  }
+}
+
+// Round to the nearest TF32 value (10 explicit mantissa bits), returned as an
+// fp32 whose 13 low mantissa bits are zero, so that the tensor core reads it
+// exactly.  Rounding (not truncation) leaves the split errors unbiased.
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+// x = h + l exactly up to l's own rounding: h = tf32(x), l = tf32(x - h)
+// (x - h is exact in fp32; |l| <= 2^-11 |x|, its rounding error <= 2^-23 |x|).
+__device__ __forceinline__ void tf32_split(float x, float& h, float& l) {
+  h = tf32_rna(x);
+  l = tf32_rna(x - h);
+}
+
+template <int PM>
+__device__ __forceinline__ float relu_pow(float z, float p) {
+  const float x = fmaxf(z, 0.0f);
+  if constexpr (PM == POW_1) return x;
+  if constexpr (PM == POW_2) return x * x;
+  if constexpr (PM == POW_3) return x * x * x;
+  return x > 0.0f ? expf(p * logf(x + 1e-10f)) : 0.0f;
+}
+
+// ------------------------------------------------------------------ pre-pass
+// One warp per padded row of a (BH, S, 64) fp32 array: h / l copies and the
+// row's coefficients (see the file comment).  Rows S..S_pad-1 get zeros.
+__global__ void __launch_bounds__(256) tf32_split_rows_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                                              float* __restrict__ lo, float* __restrict__ r1,
+                                                              float* __restrict__ r2, int BH, int S, int S_pad,
+                                                              int is_query, int normalize, float beta) {
+  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= static_cast<int64_t>(BH) * S_pad) return;
+  const int64_t bh = row / S_pad;
+  const int i = static_cast<int>(row % S_pad);
+  if (i >= S) {
+    if (lane == 0) {
+      r1[row] = 0.0f;
+      if (is_query) r2[row] = 0.0f;
+    }
+    return;
+  }
+  const size_t off = (static_cast<size_t>(bh) * S + i) * kD + 2 * lane;
+  const float2 v = *reinterpret_cast<const float2*>(x + off);
+  float hx, lx, hy, ly;
+  tf32_split(v.x, hx, lx);
+  tf32_split(v.y, hy, ly);
+  *reinterpret_cast<float2*>(hi + off) = make_float2(hx, hy);
+  *reinterpret_cast<float2*>(lo + off) = make_float2(lx, ly);
+  float ss = fmaf(v.x, v.x, v.y * v.y);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) {
+    const float m = normalize ? fmaxf(sqrtf(ss), 1e-12f) : 1.0f;
+    r1[row] = 1.0f / m;
+    if (is_query) {
+      const float tau = beta * sqrtf((2.0f * logf(static_cast<float>(i + 1))) / static_cast<float>(kD));
+      r2[row] = tau * m;
+    }
+  }
+}
+
+// v (BH, S, 64) -> V^T h / l copies (BH, 64, S_pad), zero for keys >= S.
+// Block (32, 8) threads, one 32-key slab of one (batch, head).
+__global__ void __launch_bounds__(256) tf32_split_vt_kernel(const float* __restrict__ v, float* __restrict__ vth,
+                                                            float* __restrict__ vtl, int S, int S_pad) {
+  __shared__ float t[32][kD + 1];
+  const int64_t bh = blockIdx.y;
+  const int k0 = blockIdx.x * 32;
+  for (int r = threadIdx.y; r < 32; r += 8)
+    for (int c = threadIdx.x; c < kD; c += 32) {
+      const int key = k0 + r;
+      t[r][c] = key < S ? v[(static_cast<size_t>(bh) * S + key) * kD + c] : 0.0f;
+    }
+  __syncthreads();
+  for (int d = threadIdx.y; d < kD; d += 8) {
+    const int key = k0 + threadIdx.x;
+    float h, l;
+    tf32_split(t[threadIdx.x][d], h, l);
+    const size_t o = (static_cast<size_t>(bh) * kD + d) * S_pad + key;
+    vth[o] = h;
+    vtl[o] = l;
+  }
+}
+
+// ------------------------------------------------------------------ roles
+__device__ void tf_producer(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const WaitCtl& ctl, int bh, int m0,
+                            int n_kt) {
+  const int T = p.n_br * n_kt;
+  int q_n = 0, k_n = 0, v_n = 0;
+  bool ok = true;
+  auto load_q = [&](int br) {
+    mbar_arrive_expect_tx(&b->q_full, 2 * kQBytes);
+    for (int cb = 0; cb < 2; ++cb)
+      for (int h = 0; h < 2; ++h) {
+        tma_load_3d(smem + kOffQh + cb * 2 * kBox + h * kBox, &p.tm_qh[br], &b->q_full, 32 * cb, m0 + 64 * h, bh);
+        tma_load_3d(smem + kOffQl + cb * 2 * kBox + h * kBox, &p.tm_ql[br], &b->q_full, 32 * cb, m0 + 64 * h, bh);
+      }
+    ++q_n;
+  };
+  load_q(0);
+  for (int t = 0; t < T && ok; ++t) {
+    const int br = t / n_kt, j = t % n_kt, e = t & 1, u = t >> 1;
+    if (j == 0 && br > 0) {
+      ok = mbar_wait(&b->q_empty, (br - 1) & 1, ctl, ST_TF_PROD);
+      if (!ok) break;
+      load_q(br);
+    }
+    if (u > 0 && !(ok = mbar_wait(&b->k_empty[e], (u - 1) & 1, ctl, ST_TF_PROD))) break;
+    uint8_t* kd = smem + kOffK + e * 2 * kKBytes;
+    mbar_arrive_expect_tx(&b->k_full[e], 2 * kKBytes);
+    for (int cb = 0; cb < 2; ++cb) {
+      tma_load_3d(kd + cb * kBox, &p.tm_kh[br], &b->k_full[e], 32 * cb, kBN * j, bh);
+      tma_load_3d(kd + kKBytes + cb * kBox, &p.tm_kl[br], &b->k_full[e], 32 * cb, kBN * j, bh);
+    }
+    ++k_n;
+    if (u > 0 && !(ok = mbar_wait(&b->v_empty[e], (u - 1) & 1, ctl, ST_TF_PROD))) break;
+    uint8_t* vd = smem + kOffV + e * 2 * kKBytes;
+    mbar_arrive_expect_tx(&b->v_full[e], 2 * kKBytes);
+    for (int cb = 0; cb < 2; ++cb) {
+      tma_load_3d(vd + cb * kBox, &p.tm_vh, &b->v_full[e], kBN * j + 32 * cb, 0, bh);
+      tma_load_3d(vd + kKBytes + cb * kBox, &p.tm_vl, &b->v_full[e], kBN * j + 32 * cb, 0, bh);
+    }
+    ++v_n;
+  }
+  if (!ok) {  // let the copies already issued land before the CTA exits
+    tf_drain_wait(&b->q_full, (q_n - 1) & 1, ctl);
+    for (int i = k_n > 2 ? k_n - 2 : 0; i < k_n; ++i) tf_drain_wait(&b->k_full[i & 1], (i >> 1) & 1, ctl);
+    for (int i = v_n > 2 ? v_n - 2 : 0; i < v_n; ++i) tf_drain_wait(&b->v_full[i & 1], (i >> 1) & 1, ctl);
+  }
+}
+
+__device__ void tf_mma(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const WaitCtl& ctl, uint32_t tmem,
+                       int n_kt) {
+  const int T = p.n_br * n_kt;
+  const uint32_t qh = smem_u32(smem + kOffQh), ql = smem_u32(smem + kOffQl);
+  bool ok = mbar_wait(&b->q_full, 0, ctl, ST_TF_MMA);
+  tc_fence_after();
+  auto qk = [&](int t) {
+    const int br = t / n_kt, j = t % n_kt, e = t & 1, u = t >> 1;
+    if (j == 0 && br > 0) {
+      if (!(ok = mbar_wait(&b->q_full, br & 1, ctl, ST_TF_MMA))) return;
+      tc_fence_after();
+    }
+    if (!(ok = mbar_wait(&b->k_full[e], u & 1, ctl, ST_TF_MMA))) return;
+    tc_fence_after();
+    const uint32_t kh = smem_u32(smem + kOffK + e * 2 * kKBytes), kl = kh + kKBytes;
+    const uint32_t d = tmem + col_s(e);
+#pragma unroll
+    for (int kk = 0; kk < kD / 8; ++kk) {
+      // k step of 8 fp32 = 32 B inside a 128-B swizzled row; column box kk / 4
+      const uint32_t oq = (kk >> 2) * 2 * kBox + (kk & 3) * 32, ok_ = (kk >> 2) * kBox + (kk & 3) * 32;
+      const uint64_t aqh = smem_desc_sw128(qh + oq, 16, 1024), aql = smem_desc_sw128(ql + oq, 16, 1024);
+      const uint64_t bkh = smem_desc_sw128(kh + ok_, 16, 1024), bkl = smem_desc_sw128(kl + ok_, 16, 1024);
+      // h*h products and the two cross terms go to separate accumulators so
+      // that the small terms are not added onto the large partial sums
+      mma_ss_tf32(d, aqh, bkh, kk > 0 ? 1u : 0u);
+      mma_ss_tf32(d + 64, aqh, bkl, kk > 0 ? 1u : 0u);
+      mma_ss_tf32(d + 64, aql, bkh, 1u);
+    }
+    tc_commit(&b->k_empty[e]);
+    tc_commit(&b->s_full[e]);
+    if (j == n_kt - 1 && br + 1 < p.n_br) tc_commit(&b->q_empty);
+  };
+  // Each tile's P V goes into a fresh partial O (slot t % 2) that the
+  // transform threads add into fp32 registers: the tensor core accumulates
+  // 24 products per tile instead of the whole key range.
+  auto pv = [&](int t) {
+    const int e = t & 1, u = t >> 1;
+    if (!(ok = mbar_wait(&b->v_full[e], u & 1, ctl, ST_TF_MMA))) return;
+    if (!(ok = mbar_wait(&b->p_full[e], u & 1, ctl, ST_TF_MMA))) return;
+    if (u > 0 && !(ok = mbar_wait(&b->o_free[e], (u - 1) & 1, ctl, ST_TF_MMA))) return;
+    tc_fence_after();
+    const uint32_t vh = smem_u32(smem + kOffV + e * 2 * kKBytes), vl = vh + kKBytes;
+#pragma unroll
+    for (int kk = 0; kk < kBN / 8; ++kk) {
+      const uint32_t ov = (kk >> 2) * kBox + (kk & 3) * 32;
+      const uint64_t bvh = smem_desc_sw128(vh + ov, 16, 1024), bvl = smem_desc_sw128(vl + ov, 16, 1024);
+      const uint32_t ah = tmem + col_s(e) + 8 * kk, al = tmem + col_pl(e) + 8 * kk;
+      const uint32_t d = tmem + kColO + 128 * e;
+      mma_ts_tf32(d, ah, bvh, kk > 0 ? 1u : 0u);
+      mma_ts_tf32(d + 64, ah, bvl, kk > 0 ? 1u : 0u);
+      mma_ts_tf32(d + 64, al, bvh, 1u);
+    }
+    tc_commit(&b->v_empty[e]);
+    tc_commit(&b->o_full[e]);
+  };
+  if (ok) qk(0);
+  if (ok && T > 1) qk(1);
+  for (int t = 0; t < T && ok; ++t) {
+    pv(t);
+    if (ok && t + 2 < T) qk(t + 2);
+  }
+  if (!ok) {  // let every MMA this thread issued finish before TMEM is freed
+    tc_commit(&b->drain);
+    tf_drain_wait(&b->drain, 0, ctl);
+  }
+}
+
+template <int PM>
+__device__ void tf_transform(const Tf32FwdParams& p, Tf32Bars* b, const WaitCtl& ctl, uint32_t tmem, int bh, int m0,
+                             int n_kt, int warp, int lane) {
+  const int quarter = warp & 3;
+  const int row = 32 * quarter + lane;
+  const int gi = m0 + row;
+  const uint32_t tl = tmem + (static_cast<uint32_t>(32 * quarter) << 16);
+  const int T = p.n_br * n_kt;
+  const size_t rbase = static_cast<size_t>(bh) * p.S_pad;
+  float rq = 0.0f, tq = 0.0f, w = 1.0f;
+  float acc[kD];
+#pragma unroll
+  for (int c = 0; c < kD; ++c) acc[c] = 0.0f;
+  bool ok = true;
+  // add tile x's partial O (TMEM slot x % 2) into acc and release the slot
+  auto harvest = [&](int x) {
+    const int e = x & 1, u = x >> 1;
+    if (!(ok = mbar_wait_warp(&b->o_full[e], u & 1, ctl, ST_TF_TR))) return;
+    tc_fence_after();
+#pragma unroll
+    for (int c2 = 0; c2 < 2; ++c2) {
+      uint32_t ob[32], os[32];
+      tmem_ld32(tl + kColO + 128 * e + 32 * c2, ob);
+      tmem_ld32(tl + kColO + 128 * e + 64 + 32 * c2, os);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 32; ++c) acc[32 * c2 + c] += __uint_as_float(ob[c]) + __uint_as_float(os[c]);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b->o_free[e]);
+  };
+  for (int t = 0; t < T; ++t) {
+    const int br = t / n_kt, j = t % n_kt, e = t & 1, u = t >> 1;
+    if (j == 0) {
+      w = br ? -p.lam : 1.0f;
+      rq = gi < p.S ? p.rq[br][rbase + gi] : 0.0f;  // rows past S: z = 0, P = 0
+      tq = gi < p.S ? p.tq[br][rbase + gi] : 0.0f;
+    }
+    const float* rk = p.rk[br] + rbase + kBN * j;
+    if (!(ok = mbar_wait_warp(&b->s_full[e], u & 1, ctl, ST_TF_TR))) break;
+    tc_fence_after();
+    const bool diag = kBN * j + kBN - 1 > m0;  // some key of the tile lies past some row
+#pragma unroll
+    for (int c2 = 0; c2 < 2; ++c2) {
+      uint32_t s[32], sl[32];
+      tmem_ld32(tl + col_s(e) + 32 * c2, s);
+      tmem_ld32(tl + col_pl(e) + 32 * c2, sl);
+      tmem_wait_ld();
+      uint32_t hi[32], lo[32];
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) {
+        const float4 r4 = *reinterpret_cast<const float4*>(rk + 32 * c2 + 4 * c4);
+        const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = 4 * c4 + q;
+          float sv = __uint_as_float(s[c]) + __uint_as_float(sl[c]);
+          if (diag && kBN * j + 32 * c2 + c > gi) sv = 0.0f;  // causal mask to zero
+          const float pv = w * relu_pow<PM>(fmaf(sv, rr[q], -tq) * rq, p.relu_power);
+          float h, l;
+          tf32_split(pv, h, l);
+          hi[c] = __float_as_uint(h);
+          lo[c] = __float_as_uint(l);
+        }
+      }
+      tmem_st32(tl + col_s(e) + 32 * c2, hi);
+      tmem_st32(tl + col_pl(e) + 32 * c2, lo);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&b->p_full[e]);
+    if (t > 0) {
+      harvest(t - 1);
+      if (!ok) break;
+    }
+  }
+  if (ok) harvest(T - 1);
+  if (!ok || gi >= p.S) return;
+  float* dst = p.out + (static_cast<size_t>(bh) * p.S + gi) * kD;
+#pragma unroll
+  for (int c4 = 0; c4 < kD / 4; ++c4)
+    *reinterpret_cast<float4*>(dst + 4 * c4) = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
+}
+
+template <int PM>
+__global__ void __launch_bounds__(kThreads, 1) tda_tf32_fwd_kernel(const __grid_constant__ Tf32FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Tf32Bars* b = reinterpret_cast<Tf32Bars*>(smem + kOffBar);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // longest query tiles (most key tiles) first
+  const int qt = p.n_qt - 1 - static_cast<int>(blockIdx.x / p.BH);
+  const int bh = static_cast<int>(blockIdx.x % p.BH);
+  const int m0 = kBM * qt;
+  const int n_kt = p.causal_skip ? min(2 * qt + 2, p.n_kt_all) : p.n_kt_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&b->q_full, 1);
+    mbar_init(&b->q_empty, 1);
+    mbar_init(&b->drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&b->k_full[i], 1);
+      mbar_init(&b->k_empty[i], 1);
+      mbar_init(&b->v_full[i], 1);
+      mbar_init(&b->v_empty[i], 1);
+      mbar_init(&b->s_full[i], 1);
+      mbar_init(&b->p_full[i], 4);
+      mbar_init(&b->o_full[i], 1);
+      mbar_init(&b->o_free[i], 4);
+    }
+    b->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&b->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = b->tmem_base;
+  const WaitCtl ctl{&b->abort_flag, p.status, p.timeout_ns};
+  if (warp == 0) {
+    if (lane == 0) tf_producer(p, smem, b, ctl, bh, m0, n_kt);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) tf_mma(p, smem, b, ctl, tmem, n_kt);
+    __syncwarp();
+  } else {
+    tf_transform<PM>(p, b, ctl, tmem, bh, m0, n_kt, warp, lane);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_tf32_split(const float* const q[2], const float* const k[2], const float* v,
+                              const Tf32Workspace& ws, int n_br, int BH, int S, float beta, int normalize,
+                              cudaStream_t stream) {
+  const int S_pad = static_cast<int>(tf32_padded_seq(S));
+  const int64_t rows = static_cast<int64_t>(BH) * S_pad;
+  const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+  for (int br = 0; br < n_br; ++br) {
+    tf32_split_rows_kernel<<<grid, 256, 0, stream>>>(q[br], ws.qh[br], ws.ql[br], ws.rq[br], ws.tq[br], BH, S,
+                                                     S_pad, 1, normalize, beta);
+    tf32_split_rows_kernel<<<grid, 256, 0, stream>>>(k[br], ws.kh[br], ws.kl[br], ws.rk[br], nullptr, BH, S, S_pad,
+                                                     0, normalize, beta);
+  }
+  tf32_split_vt_kernel<<<dim3(S_pad / 32, BH), dim3(32, 8), 0, stream>>>(v, ws.vth, ws.vtl, S, S_pad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tf32_fwd(const Tf32FwdParams& p, int pow_mode, cudaStream_t stream) {
+  void (*kern)(Tf32FwdParams);
+  switch (pow_mode) {
+    case POW_1: kern = tda_tf32_fwd_kernel<POW_1>; break;
+    case POW_2: kern = tda_tf32_fwd_kernel<POW_2>; break;
+    case POW_3: kern = tda_tf32_fwd_kernel<POW_3>; break;
+    default: kern = tda_tf32_fwd_kernel<POW_GENERAL>; break;
+  }
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = static_cast<unsigned>(p.BH) * static_cast<unsigned>(p.n_qt);
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace tda

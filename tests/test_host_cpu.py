@@ -44,7 +44,11 @@ def test_library_host_only_calls():
     assert lib.tda_workspace_size(0, _lib.TDA_BF16, 2, 100, 64, 1) == 1280
     assert lib.tda_workspace_size(1, _lib.TDA_BF16, 2, 100, 64, 1) == 2560
     assert lib.tda_workspace_size(1, _lib.TDA_BF16, 2, 100, 64, 0) == 0
-    assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 64, 1) == 0
+    # fp32 at head_dim 64: TF32 high / low copies of q, k (2 x 51200 B each), three
+    # per-row coefficient arrays (1024 B each, seq padded to 128) and V^T high / low (65536 B each)
+    assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 64, 1) == 4 * 51200 + 3 * 1024 + 2 * 65536
+    assert lib.tda_workspace_size(1, _lib.TDA_F32, 2, 100, 64, 0) == 8 * 51200 + 6 * 1024 + 2 * 65536
+    assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 128, 1) == 0
 
 
 def test_library_rejects_bad_arguments_without_launching():
