@@ -302,7 +302,7 @@ int tda_debug_set(int inject, uint64_t wait_timeout_ns) {
 
 size_t tda_workspace_size(int differential, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim,
                           int normalize) {
-  if (dtype == TDA_F32 && head_dim == 64 && batch_heads >= 1 && batch_heads <= 65535 && seq_len >= 1)
+  if (dtype == TDA_F32 && head_dim == 64 && batch_heads >= 1 && seq_len >= 1)
     return tf32_bytes(batch_heads, seq_len, differential != 0);
   if (!normalize || !tc_supported(dtype, head_dim) || batch_heads < 1 || seq_len < 1) return 0;
   const size_t one = (rk_bytes(batch_heads, seq_len) + 255) / 256 * 256;
@@ -413,7 +413,7 @@ int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dty
                  int normalize, void* workspace, size_t workspace_bytes, int* status, void* stream) {
   if (dtype == TDA_F32) {
     if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
-    if (head_dim == 64 && workspace && batch_heads >= 1 && batch_heads <= 65535 && seq_len >= 1 &&
+    if (head_dim == 64 && workspace && batch_heads >= 1 && seq_len >= 1 &&
         workspace_bytes >= tf32_bytes(batch_heads, seq_len, false))
       return run_tf32(q, nullptr, k, nullptr, v, out, batch_heads, seq_len, beta, 0.0f, relu_power, normalize,
                       workspace, status, stream, false);
@@ -442,7 +442,7 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                  int* status, void* stream) {
   if (dtype == TDA_F32) {
     if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
-    if (head_dim == 64 && workspace && batch_heads >= 1 && batch_heads <= 65535 && seq_len >= 1 &&
+    if (head_dim == 64 && workspace && batch_heads >= 1 && seq_len >= 1 &&
         workspace_bytes >= tf32_bytes(batch_heads, seq_len, true))
       return run_tf32(q1, q2, k1, k2, v, out, batch_heads, seq_len, beta, clamp01(lambda_param), relu_power,
                       normalize, workspace, status, stream, true);

@@ -13,7 +13,7 @@
 // incl. exp(p*log(x+1e-10))) and its differential wrapper (:489-519: both
 // branches accumulate into one output, the second weighted by -clamp(lambda)).
 //
-// Pre-pass (stream-ordered, into the caller's workspace):
+// Pre-pass (one stream-ordered launch, into the caller's workspace):
 //   q, k rows -> h, l copies [BH][S][64], and per row 1/m, tau*m (queries) or
 //   1/m (keys), m = max(||x||, 1e-12) when normalized, m = 1 otherwise;
 //   v -> transposed h, l copies [BH][64][S_pad] (zero past S), so that V^T is
@@ -134,64 +134,86 @@ __device__ __forceinline__ float relu_pow(float z, float p) {
 }
 
 // ------------------------------------------------------------------ pre-pass
-// One warp per padded row of a (BH, S, 64) fp32 array: h / l copies and the
-// row's coefficients (see the file comment).  Rows S..S_pad-1 get zeros.
-__global__ void __launch_bounds__(256) tf32_split_rows_kernel(const float* __restrict__ x, float* __restrict__ hi,
-                                                              float* __restrict__ lo, float* __restrict__ r1,
-                                                              float* __restrict__ r2, int BH, int S, int S_pad,
-                                                              int is_query, int normalize, float beta) {
-  const int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= static_cast<int64_t>(BH) * S_pad) return;
-  const int64_t bh = row / S_pad;
-  const int i = static_cast<int>(row % S_pad);
-  if (i >= S) {
-    if (lane == 0) {
-      r1[row] = 0.0f;
-      if (is_query) r2[row] = 0.0f;
+// One launch for every split: blockIdx.y = job (2 br: rows of q of branch br,
+// 2 br + 1: rows of k, 2 n_br: V^T), blockIdx.x = a 32-row slab of the padded
+// (BH * S_pad) rows (S_pad is a multiple of 64, so a slab lies in one head).
+struct Tf32SplitArgs {
+  const float* q[2];
+  const float* k[2];
+  const float* v;
+  Tf32Workspace w;
+  int S;
+  int S_pad;
+  int n_br;
+  int normalize;
+  float beta;
+};
+
+__global__ void __launch_bounds__(256) tf32_split_kernel(const __grid_constant__ Tf32SplitArgs a) {
+  __shared__ float t[32][kD + 1];
+  const int job = blockIdx.y;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * 32;
+  const int64_t bh = row0 / a.S_pad;
+  const int i0 = static_cast<int>(row0 % a.S_pad);
+  if (job < 2 * a.n_br) {
+    // rows: 8 threads per row, 8 floats (two 16-byte loads) each
+    const int br = job >> 1;
+    const bool is_q = (job & 1) == 0;
+    const int r = threadIdx.x >> 3, part = threadIdx.x & 7;
+    const int i = i0 + r;
+    const int64_t row = row0 + r;
+    const bool valid = i < a.S;  // padded rows get zero coefficients; every lane takes part in the shuffles
+    float* r1 = is_q ? a.w.rq[br] : a.w.rk[br];
+    const size_t off = (static_cast<size_t>(bh) * a.S + (valid ? i : 0)) * kD + 8 * part;
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+    if (valid) {
+      const float* x = (is_q ? a.q[br] : a.k[br]) + off;
+      v0 = *reinterpret_cast<const float4*>(x);
+      v1 = *reinterpret_cast<const float4*>(x + 4);
+    }
+    const float xv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float h[8], l[8], ss = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      tf32_split(xv[c], h[c], l[c]);
+      ss = fmaf(xv[c], xv[c], ss);
+    }
+    if (valid) {
+      float* hi = (is_q ? a.w.qh[br] : a.w.kh[br]) + off;
+      float* lo = (is_q ? a.w.ql[br] : a.w.kl[br]) + off;
+      *reinterpret_cast<float4*>(hi) = make_float4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<float4*>(hi + 4) = make_float4(h[4], h[5], h[6], h[7]);
+      *reinterpret_cast<float4*>(lo) = make_float4(l[0], l[1], l[2], l[3]);
+      *reinterpret_cast<float4*>(lo + 4) = make_float4(l[4], l[5], l[6], l[7]);
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    if (part == 0) {
+      const float m = a.normalize ? fmaxf(sqrtf(ss), 1e-12f) : 1.0f;
+      r1[row] = valid ? 1.0f / m : 0.0f;
+      if (is_q) {
+        const float tau = a.beta * sqrtf((2.0f * logf(static_cast<float>(i + 1))) / static_cast<float>(kD));
+        a.w.tq[br][row] = valid ? tau * m : 0.0f;
+      }
     }
     return;
   }
-  const size_t off = (static_cast<size_t>(bh) * S + i) * kD + 2 * lane;
-  const float2 v = *reinterpret_cast<const float2*>(x + off);
-  float hx, lx, hy, ly;
-  tf32_split(v.x, hx, lx);
-  tf32_split(v.y, hy, ly);
-  *reinterpret_cast<float2*>(hi + off) = make_float2(hx, hy);
-  *reinterpret_cast<float2*>(lo + off) = make_float2(lx, ly);
-  float ss = fmaf(v.x, v.x, v.y * v.y);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (lane == 0) {
-    const float m = normalize ? fmaxf(sqrtf(ss), 1e-12f) : 1.0f;
-    r1[row] = 1.0f / m;
-    if (is_query) {
-      const float tau = beta * sqrtf((2.0f * logf(static_cast<float>(i + 1))) / static_cast<float>(kD));
-      r2[row] = tau * m;
-    }
-  }
-}
-
-// v (BH, S, 64) -> V^T h / l copies (BH, 64, S_pad), zero for keys >= S.
-// Block (32, 8) threads, one 32-key slab of one (batch, head).
-__global__ void __launch_bounds__(256) tf32_split_vt_kernel(const float* __restrict__ v, float* __restrict__ vth,
-                                                            float* __restrict__ vtl, int S, int S_pad) {
-  __shared__ float t[32][kD + 1];
-  const int64_t bh = blockIdx.y;
-  const int k0 = blockIdx.x * 32;
-  for (int r = threadIdx.y; r < 32; r += 8)
-    for (int c = threadIdx.x; c < kD; c += 32) {
-      const int key = k0 + r;
-      t[r][c] = key < S ? v[(static_cast<size_t>(bh) * S + key) * kD + c] : 0.0f;
+  // V^T: the slab's 32 keys x 64 dims through shared memory, written as 64
+  // rows of 32 keys (zero for keys >= S)
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < 32; r += 8)
+    for (int c = tx; c < kD; c += 32) {
+      const int key = i0 + r;
+      t[r][c] = key < a.S ? a.v[(static_cast<size_t>(bh) * a.S + key) * kD + c] : 0.0f;
     }
   __syncthreads();
-  for (int d = threadIdx.y; d < kD; d += 8) {
-    const int key = k0 + threadIdx.x;
+  for (int d = ty; d < kD; d += 8) {
     float h, l;
-    tf32_split(t[threadIdx.x][d], h, l);
-    const size_t o = (static_cast<size_t>(bh) * kD + d) * S_pad + key;
-    vth[o] = h;
-    vtl[o] = l;
+    tf32_split(t[tx][d], h, l);
+    const size_t o = (static_cast<size_t>(bh) * kD + d) * a.S_pad + i0 + tx;
+    a.w.vth[o] = h;
+    a.w.vtl[o] = l;
   }
 }
 
@@ -352,8 +374,13 @@ __device__ void tf_transform(const Tf32FwdParams& p, Tf32Bars* b, const WaitCtl&
     if (!(ok = mbar_wait_warp(&b->s_full[e], u & 1, ctl, ST_TF_TR))) break;
     tc_fence_after();
     const bool diag = kBN * j + kBN - 1 > m0;  // some key of the tile lies past some row
-#pragma unroll
+    // rolled: one copy of the 32-key body keeps the loop inside the SM's
+    // instruction cache (unrolled, instruction fetch was the main stall)
+#pragma unroll 1
     for (int c2 = 0; c2 < 2; ++c2) {
+      float4 rk4[8];  // key coefficients of this chunk, loaded before the TMEM wait
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4) rk4[c4] = *reinterpret_cast<const float4*>(rk + 32 * c2 + 4 * c4);
       uint32_t s[32], sl[32];
       tmem_ld32(tl + col_s(e) + 32 * c2, s);
       tmem_ld32(tl + col_pl(e) + 32 * c2, sl);
@@ -361,8 +388,7 @@ __device__ void tf_transform(const Tf32FwdParams& p, Tf32Bars* b, const WaitCtl&
       uint32_t hi[32], lo[32];
 #pragma unroll
       for (int c4 = 0; c4 < 8; ++c4) {
-        const float4 r4 = *reinterpret_cast<const float4*>(rk + 32 * c2 + 4 * c4);
-        const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
+        const float rr[4] = {rk4[c4].x, rk4[c4].y, rk4[c4].z, rk4[c4].w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int c = 4 * c4 + q;
@@ -455,16 +481,20 @@ __global__ void __launch_bounds__(kThreads, 1) tda_tf32_fwd_kernel(const __grid_
 cudaError_t launch_tf32_split(const float* const q[2], const float* const k[2], const float* v,
                               const Tf32Workspace& ws, int n_br, int BH, int S, float beta, int normalize,
                               cudaStream_t stream) {
-  const int S_pad = static_cast<int>(tf32_padded_seq(S));
-  const int64_t rows = static_cast<int64_t>(BH) * S_pad;
-  const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
-  for (int br = 0; br < n_br; ++br) {
-    tf32_split_rows_kernel<<<grid, 256, 0, stream>>>(q[br], ws.qh[br], ws.ql[br], ws.rq[br], ws.tq[br], BH, S,
-                                                     S_pad, 1, normalize, beta);
-    tf32_split_rows_kernel<<<grid, 256, 0, stream>>>(k[br], ws.kh[br], ws.kl[br], ws.rk[br], nullptr, BH, S, S_pad,
-                                                     0, normalize, beta);
+  Tf32SplitArgs a;
+  for (int br = 0; br < 2; ++br) {
+    a.q[br] = q[br];
+    a.k[br] = k[br];
   }
-  tf32_split_vt_kernel<<<dim3(S_pad / 32, BH), dim3(32, 8), 0, stream>>>(v, ws.vth, ws.vtl, S, S_pad);
+  a.v = v;
+  a.w = ws;
+  a.S = S;
+  a.S_pad = static_cast<int>(tf32_padded_seq(S));
+  a.n_br = n_br;
+  a.normalize = normalize;
+  a.beta = beta;
+  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(BH) * a.S_pad / 32), static_cast<unsigned>(2 * n_br + 1));
+  tf32_split_kernel<<<grid, 256, 0, stream>>>(a);
   return cudaGetLastError();
 }
 
