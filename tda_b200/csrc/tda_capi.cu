@@ -275,6 +275,7 @@ int run_tf32(const void* q1, const void* q2, const void* k1, const void* k2, con
   prm.relu_power = p;
   prm.lam = lam;
   prm.timeout_ns = g_timeout_ns.load();
+  prm.inject = g_inject.load();
   ce = tda::launch_tf32_fwd(prm, tda::pow_mode_of(p), st);
   if (ce != cudaSuccess) return cuda_fail(ce, "fp32 tensor-core forward launch");
   return TDA_OK;

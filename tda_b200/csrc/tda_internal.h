@@ -153,6 +153,7 @@ struct Tf32FwdParams {
   float relu_power;
   float lam;      // clamped lambda (second branch weight -lam)
   unsigned long long timeout_ns;
+  int inject;     // test hook: bit 0 = producer never loads Q (forces a timeout)
 };
 
 cudaError_t launch_tf32_split(const float* const q[2], const float* const k[2], const float* v,

@@ -232,7 +232,7 @@ __device__ void tf_producer(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, 
       }
     ++q_n;
   };
-  load_q(0);
+  if (!(p.inject & 1)) load_q(0);  // test hook: with bit 0 set the first Q tile never arrives
   for (int t = 0; t < T && ok; ++t) {
     const int br = t / n_kt, j = t % n_kt, e = t & 1, u = t >> 1;
     if (j == 0 && br > 0) {
@@ -258,7 +258,7 @@ __device__ void tf_producer(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, 
     ++v_n;
   }
   if (!ok) {  // let the copies already issued land before the CTA exits
-    tf_drain_wait(&b->q_full, (q_n - 1) & 1, ctl);
+    if (q_n > 0) tf_drain_wait(&b->q_full, (q_n - 1) & 1, ctl);
     for (int i = k_n > 2 ? k_n - 2 : 0; i < k_n; ++i) tf_drain_wait(&b->k_full[i & 1], (i >> 1) & 1, ctl);
     for (int i = v_n > 2 ? v_n - 2 : 0; i < v_n; ++i) tf_drain_wait(&b->v_full[i & 1], (i >> 1) & 1, ctl);
   }

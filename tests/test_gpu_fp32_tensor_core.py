@@ -96,3 +96,25 @@ def test_public_api_fp32_head_dim_64_uses_workspace_path():
     ref = O.diff_fwd(*xn, 1.0, 0.5, 2.0, True)
     assert out.dtype == torch.float32
     assert O.rel_l2(out.cpu().numpy(), ref) <= TOL_F32
+
+
+def test_timeout_reports_status_and_context_survives():
+    """Failure detection of the fp32 tensor-core kernel without a GPU fault:
+    the test hook makes its producer skip the first Q load, every bounded wait
+    gives up after 50 ms, the kernel frees its tensor memory and reports a
+    status the host reads; the next call on the same context is correct."""
+    lib = _lib.load()
+    BH, S = 2, 300
+    g = torch.Generator().manual_seed(21)
+    xs_h = [torch.randn((BH, S, 64), generator=g) for _ in range(5)]
+    xs = [x.to(DEV) for x in xs_h]
+    lib.tda_debug_set(1, 50_000_000)
+    try:
+        with pytest.raises(_lib.TdaError, match="status"):
+            _run(lib, xs, BH, S, 1.0, 0.5, 2.0, True, True, True)
+    finally:
+        lib.tda_debug_set(0, 0)
+    ops.check_status()  # cleared by the failed check
+    out = _run(lib, xs, BH, S, 1.0, 0.5, 2.0, True, True, True)
+    ref = O.diff_fwd(*[x.numpy()[None] for x in xs_h], 1.0, 0.5, 2.0, True)[0]
+    assert O.rel_l2(out, ref) <= TOL_F32
