@@ -80,6 +80,13 @@ def flops_of(op, bh, S, D):
     return (3.0 if op == "diff" else 2.0) * bh * float(S) ** 2 * D
 
 
+def bwd_flops_of(op, bh, S, D):
+    """Dense causal algorithmic backward FLOPs: per branch five GEMMs of
+    2*S*S*D/2 per (batch, head) (recomputed S, dP = dout V^T, dV = P^T dout,
+    dQ = dA K, dK = dA^T Q), twice for the differential form."""
+    return (10.0 if op == "diff" else 5.0) * bh * float(S) ** 2 * D
+
+
 def describe(name):
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
     lam_s = f" lambda={lam}" if op == "diff" else ""
@@ -274,23 +281,42 @@ def run_reference_triton(args, rank, local, world):
                 return ref.threshold_rela_triton(F.normalize(q, dim=-1), F.normalize(k, dim=-1), v, bt, p)
             return ref.threshold_rela_triton(q, k, v, bt, p)
 
+    timed = step
+    if args.backward:
+        # the reference's autograd backward (its ThresholdRelaFunction.backward
+        # kernels, T.py:118-324 / :405-469, plus F.normalize's and the combine's
+        # gradients) for the same upstream gradient as the tda arm's --backward
+        xs_g = [x.detach().requires_grad_(True) for x in xs]
+        if op == "diff":
+            out = ref.differential_threshold_rela_triton(*xs_g, bt, lt, p, norm)
+        elif norm:
+            out = ref.threshold_rela_triton(F.normalize(xs_g[0], dim=-1), F.normalize(xs_g[1], dim=-1), xs_g[2], bt, p)
+        else:
+            out = ref.threshold_rela_triton(*xs_g, bt, p)
+        g = torch.Generator(device=dev).manual_seed(777)
+        dout = torch.randn(out.shape, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16).to(out.dtype)
+
+        def timed():
+            torch.autograd.backward(out, dout, retain_graph=True)
+
     for _ in range(args.warmup):
-        step()
+        timed()
     torch.cuda.synchronize()
     ms = []
     for _ in range(args.steps):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        step()
+        timed()
         b.record()
         torch.cuda.synchronize()
         ms.append(a.elapsed_time(b))
     total = sum(ms)
-    flops = flops_of(op, B * H, S, D)
+    flops = bwd_flops_of(op, B * H, S, D) if args.backward else flops_of(op, B * H, S, D)
     val = flops * args.steps / (total * 1e-3) / 1e12
     line = {
-        "metric": METRIC, "value": val, "unit": "TFLOP/s", "impl": "reference-triton", "n_gpus": 1,
+        "metric": f"TDA backward TFLOP/s ({name})" if args.backward else METRIC, "value": val, "unit": "TFLOP/s",
+        "impl": "reference-triton", "pass": "backward" if args.backward else "forward", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32 (TF32 dots)",
         "data": "synthetic",
@@ -312,7 +338,6 @@ def run_tda_backward(args, rank, local, world):
     import torch.distributed as dist
     from datetime import timedelta
 
-    from oracle.tda_oracle import bwd_flops
     from tda_b200 import _lib
     from tda_b200.shard import max_over_ranks, shard_range
 
@@ -374,7 +399,7 @@ def run_tda_backward(args, rank, local, world):
     barrier()
     clk = clocks.stop() if clocks else None
     ms = max_over_ranks(e0.elapsed_time(e1), dev)
-    fl = bwd_flops(B * H, S, D, op == "diff")
+    fl = bwd_flops_of(op, B * H, S, D)
     value = fl * args.steps / (ms / 1e3) / 1e12
     peaks, peak_src = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
@@ -383,7 +408,7 @@ def run_tda_backward(args, rank, local, world):
         peak = 148 * 128 * 2 * 1.965e9 / 1e12
         peak_note = "nominal FFMA peak, 148 SMs x 128 lanes x 2 x 1.965 GHz"
     ops.check_status(dev)
-    achieved = bwd_flops(n_bh, S, D, op == "diff") * args.steps / (e0.elapsed_time(e1) / 1e3) / 1e12
+    achieved = bwd_flops_of(op, n_bh, S, D) * args.steps / (e0.elapsed_time(e1) / 1e3) / 1e12
     if rank == 0:
         line = {
             "metric": f"TDA backward TFLOP/s ({name})", "value": value, "unit": "TFLOP/s", "impl": "tda",
