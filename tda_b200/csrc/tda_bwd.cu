@@ -94,10 +94,21 @@ __device__ __forceinline__ void load_rows(float* dst, int ld, const T* src, int 
 template <int D>
 __device__ __forceinline__ void normalize_rows(float* tile, float* rinv) {
   using C = BwdCfg<D>;
-  if (threadIdx.x < BT) {
+  {
+    // four adjacent lanes per row, D/4 dims each
+    const int row = threadIdx.x >> 2, part = threadIdx.x & 3;
     float ss = 0.f;
-    for (int d = 0; d < D; ++d) ss = fmaf(tile[threadIdx.x * C::LD + d], tile[threadIdx.x * C::LD + d], ss);
-    rinv[threadIdx.x] = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+#pragma unroll
+    for (int d = part * (D / 4); d < (part + 1) * (D / 4); d += 4) {
+      const float4 x = *reinterpret_cast<const float4*>(tile + row * C::LD + d);
+      ss = fmaf(x.x, x.x, ss);
+      ss = fmaf(x.y, x.y, ss);
+      ss = fmaf(x.z, x.z, ss);
+      ss = fmaf(x.w, x.w, ss);
+    }
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    if (part == 0) rinv[row] = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < BT * D; idx += kThreads) {
@@ -152,29 +163,35 @@ template <int D>
 __device__ __forceinline__ void mac_rows(float (&acc)[4][BwdCfg<D>::CPT], const float* M, const float* X, int ty,
                                          int tx) {
   using C = BwdCfg<D>;
-#pragma unroll 4
-  for (int j = 0; j < BT; ++j) {
-    float m[4];
+#pragma unroll 2
+  for (int j = 0; j < BT; j += 4) {
+    float4 m4[4];  // four j per 16-byte load of each row of M
 #pragma unroll
-    for (int i = 0; i < 4; ++i) m[i] = M[(ty + 16 * i) * LDP + j];
-    if constexpr (D >= 64) {
+    for (int i = 0; i < 4; ++i) m4[i] = *reinterpret_cast<const float4*>(M + (ty + 16 * i) * LDP + j);
 #pragma unroll
-      for (int g = 0; g < D / 64; ++g) {
-        const float4 x = *reinterpret_cast<const float4*>(X + j * C::LD + 64 * g + 4 * tx);
+    for (int jj = 0; jj < 4; ++jj) {
+      float m[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          acc[i][4 * g + 0] = fmaf(m[i], x.x, acc[i][4 * g + 0]);
-          acc[i][4 * g + 1] = fmaf(m[i], x.y, acc[i][4 * g + 1]);
-          acc[i][4 * g + 2] = fmaf(m[i], x.z, acc[i][4 * g + 2]);
-          acc[i][4 * g + 3] = fmaf(m[i], x.w, acc[i][4 * g + 3]);
+      for (int i = 0; i < 4; ++i) m[i] = jj == 0 ? m4[i].x : (jj == 1 ? m4[i].y : (jj == 2 ? m4[i].z : m4[i].w));
+      if constexpr (D >= 64) {
+#pragma unroll
+        for (int g = 0; g < D / 64; ++g) {
+          const float4 x = *reinterpret_cast<const float4*>(X + (j + jj) * C::LD + 64 * g + 4 * tx);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[i][4 * g + 0] = fmaf(m[i], x.x, acc[i][4 * g + 0]);
+            acc[i][4 * g + 1] = fmaf(m[i], x.y, acc[i][4 * g + 1]);
+            acc[i][4 * g + 2] = fmaf(m[i], x.z, acc[i][4 * g + 2]);
+            acc[i][4 * g + 3] = fmaf(m[i], x.w, acc[i][4 * g + 3]);
+          }
         }
-      }
-    } else {
+      } else {
 #pragma unroll
-      for (int t = 0; t < C::CPT; ++t) {
-        const float x = X[j * C::LD + C::CPT * tx + t];
+        for (int t = 0; t < C::CPT; ++t) {
+          const float x = X[(j + jj) * C::LD + C::CPT * tx + t];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[i][t] = fmaf(m[i], x, acc[i][t]);
+          for (int i = 0; i < 4; ++i) acc[i][t] = fmaf(m[i], x, acc[i][t]);
+        }
       }
     }
   }
