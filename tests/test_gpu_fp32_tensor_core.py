@@ -118,3 +118,30 @@ def test_timeout_reports_status_and_context_survives():
     out = _run(lib, xs, BH, S, 1.0, 0.5, 2.0, True, True, True)
     ref = O.diff_fwd(*[x.numpy()[None] for x in xs_h], 1.0, 0.5, 2.0, True)[0]
     assert O.rel_l2(out, ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("beta", [1.0, -0.5])
+def test_long_sequence_sampled_rows(beta):
+    """S = 4096 (64 key tiles accumulated per row): a sample of query rows at
+    the start, middle and end against the oracle, differential form."""
+    BH, S = 2, 4096
+    g = torch.Generator().manual_seed(4096 + int(10 * beta))
+    xs_h = [torch.randn((BH, S, 64), generator=g) for _ in range(5)]
+    xs = [x.to(DEV) for x in xs_h]
+    rows = list(range(0, 64)) + list(range(2000, 2064)) + list(range(S - 64, S))
+    lib = _lib.load()
+    out = _run(lib, xs, BH, S, beta, 0.5, 2.0, True, True, True)
+    ref = O.diff_fwd(*[x.numpy()[None] for x in xs_h], beta, 0.5, 2.0, True, rows=rows)[0]
+    assert O.rel_l2(out[:, rows], ref[:, rows]) <= TOL_F32
+
+
+def test_public_api_fp32_strided_views():
+    """(B, S, H, D) fp32 storage passed as (B, H, S, D) views: made contiguous by
+    the public API, then the tensor-core fp32 path."""
+    g = torch.Generator().manual_seed(31)
+    xs_h = [torch.randn((1, 300, 3, 64), generator=g) for _ in range(3)]
+    views = [x.to(DEV).transpose(1, 2) for x in xs_h]
+    out = ops.threshold_rela_triton(*views, torch.tensor(1.0), 2.0, True)
+    ref = O.rect_fwd(*[x.transpose(1, 2).contiguous().numpy() for x in xs_h], 1.0, 2.0, True)
+    assert out.dtype == torch.float32 and out.shape == (1, 3, 300, 64)
+    assert O.rel_l2(out.cpu().numpy(), ref) <= TOL_F32
