@@ -533,7 +533,7 @@ def run_tda(args, rank, local, world):
                                            p, int(norm), rk[0].data_ptr(), status.data_ptr(), sp))
 
     n_br = 2 if op == "diff" else 1
-    tf32 = f32 and D == 64  # fp32 on the tensor cores: one split pre-pass launch and the forward
+    tf32 = f32 and D in (64, 128)  # fp32 on the tensor cores: one split pre-pass launch and the forward
     launches_per_step = 2 if tf32 else n_br * int(norm and not f32) + 1
 
     for _ in range(args.warmup):

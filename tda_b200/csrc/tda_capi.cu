@@ -111,13 +111,13 @@ int make_map4(CUtensorMap* m, const View& x, int64_t batches, int64_t heads, int
   return TDA_OK;
 }
 
-// A contiguous fp32 array viewed as 3-D {d0, d1, d2}; box {32, 64, 1} (128 B x 64 rows); 128-B swizzle.
-int make_map_f32(CUtensorMap* m, const void* base, int64_t d0, int64_t d1, int64_t d2) {
+// A contiguous fp32 array viewed as 3-D {d0, d1, d2}; box {32, box_rows, 1} (128 B x box_rows); 128-B swizzle.
+int make_map_f32(CUtensorMap* m, const void* base, int64_t d0, int64_t d1, int64_t d2, int box_rows) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(d0 * 4), static_cast<cuuint64_t>(d0 * d1 * 4)};
-  cuuint32_t box[3] = {32, 64, 1};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -224,59 +224,62 @@ int run_simt(const void* q1, const void* q2, const void* k1, const void* k2, con
   return TDA_OK;
 }
 
-// fp32 inputs at head_dim 64 on the tensor cores (three TF32 products per
-// fp32 product): TF32 split pre-pass into the workspace, then the forward.
-size_t tf32_bytes(int64_t BH, int64_t S, bool differential) {
-  return tda::tf32_carve(nullptr, BH, S, differential ? 2 : 1).bytes;
+// fp32 inputs at head_dim 64 / 128 on the tensor cores (three TF32 products
+// per fp32 product): TF32 split pre-pass into the workspace, then the forward.
+bool tf32_supported(int64_t D) { return D == 64 || D == 128; }
+
+size_t tf32_bytes(int64_t BH, int64_t S, int64_t D, bool differential) {
+  return tda::tf32_carve(nullptr, BH, S, D, differential ? 2 : 1).bytes;
 }
 
 int run_tf32(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int64_t BH,
-             int64_t S, float beta, float lam, float p, int normalize, void* workspace, int* status, void* stream,
-             bool differential) {
-  if (int e = check_common(BH, S, 64, status)) return e;
+             int64_t S, int64_t D, float beta, float lam, float p, int normalize, void* workspace, int* status,
+             void* stream, bool differential) {
+  if (int e = check_common(BH, S, D, status)) return e;
   const void* ins[5] = {q1, k1, v, differential ? q2 : q1, differential ? k2 : k1};
   for (const void* x : ins)
     if (!x || !aligned16(x)) return fail(TDA_ERR_INVALID, "inputs must be non-NULL and 16-byte aligned");
   if (!out || !aligned16(out)) return fail(TDA_ERR_INVALID, "out must be non-NULL and 16-byte aligned");
   if (!workspace || !aligned16(workspace)) return fail(TDA_ERR_WORKSPACE, "workspace must be 16-byte aligned");
   const int n_br = differential ? 2 : 1;
-  const tda::Tf32Workspace w = tda::tf32_carve(workspace, BH, S, n_br);
+  const tda::Tf32Workspace w = tda::tf32_carve(workspace, BH, S, D, n_br);
   const float* qs[2] = {static_cast<const float*>(q1), static_cast<const float*>(differential ? q2 : q1)};
   const float* ks[2] = {static_cast<const float*>(k1), static_cast<const float*>(differential ? k2 : k1)};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t ce = tda::launch_tf32_split(qs, ks, static_cast<const float*>(v), w, n_br, static_cast<int>(BH),
-                                          static_cast<int>(S), beta, normalize, st);
+                                          static_cast<int>(S), static_cast<int>(D), beta, normalize, st);
   if (ce != cudaSuccess) return cuda_fail(ce, "fp32 split pre-pass launch");
   const int64_t S_pad = tda::tf32_padded_seq(S);
+  const int kt = tda::tf32_key_tile(static_cast<int>(D));
   tda::Tf32FwdParams prm;
   memset(&prm, 0, sizeof(prm));
   for (int br = 0; br < 2; ++br) {
     const int b = br < n_br ? br : 0;
     int e;
-    if ((e = make_map_f32(&prm.tm_qh[br], w.qh[b], 64, S, BH))) return e;
-    if ((e = make_map_f32(&prm.tm_ql[br], w.ql[b], 64, S, BH))) return e;
-    if ((e = make_map_f32(&prm.tm_kh[br], w.kh[b], 64, S, BH))) return e;
-    if ((e = make_map_f32(&prm.tm_kl[br], w.kl[b], 64, S, BH))) return e;
+    if ((e = make_map_f32(&prm.tm_qh[br], w.qh[b], D, S, BH, 64))) return e;
+    if ((e = make_map_f32(&prm.tm_ql[br], w.ql[b], D, S, BH, 64))) return e;
+    if ((e = make_map_f32(&prm.tm_kh[br], w.kh[b], D, S, BH, kt))) return e;
+    if ((e = make_map_f32(&prm.tm_kl[br], w.kl[b], D, S, BH, kt))) return e;
     prm.rq[br] = w.rq[b];
     prm.tq[br] = w.tq[b];
     prm.rk[br] = w.rk[b];
   }
-  if (int e = make_map_f32(&prm.tm_vh, w.vth, S_pad, 64, BH)) return e;
-  if (int e = make_map_f32(&prm.tm_vl, w.vtl, S_pad, 64, BH)) return e;
+  if (int e = make_map_f32(&prm.tm_vh, w.vth, S_pad, D, BH, static_cast<int>(D))) return e;
+  if (int e = make_map_f32(&prm.tm_vl, w.vtl, S_pad, D, BH, static_cast<int>(D))) return e;
   prm.out = static_cast<float*>(out);
   prm.status = status;
   prm.S = static_cast<int>(S);
   prm.S_pad = static_cast<int>(S_pad);
   prm.BH = static_cast<int>(BH);
   prm.n_qt = static_cast<int>((S + 127) / 128);
-  prm.n_kt_all = static_cast<int>(S_pad / 64);
+  prm.n_kt_all = static_cast<int>(S_pad / kt);
   prm.causal_skip = beta >= 0.0f;
   prm.n_br = n_br;
   prm.relu_power = p;
   prm.lam = lam;
   prm.timeout_ns = g_timeout_ns.load();
   prm.inject = g_inject.load();
-  ce = tda::launch_tf32_fwd(prm, tda::pow_mode_of(p), st);
+  ce = tda::launch_tf32_fwd(prm, static_cast<int>(D), tda::pow_mode_of(p), st);
   if (ce != cudaSuccess) return cuda_fail(ce, "fp32 tensor-core forward launch");
   return TDA_OK;
 }
@@ -303,8 +306,8 @@ int tda_debug_set(int inject, uint64_t wait_timeout_ns) {
 
 size_t tda_workspace_size(int differential, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim,
                           int normalize) {
-  if (dtype == TDA_F32 && head_dim == 64 && batch_heads >= 1 && seq_len >= 1)
-    return tf32_bytes(batch_heads, seq_len, differential != 0);
+  if (dtype == TDA_F32 && tf32_supported(head_dim) && batch_heads >= 1 && seq_len >= 1)
+    return tf32_bytes(batch_heads, seq_len, head_dim, differential != 0);
   if (!normalize || !tc_supported(dtype, head_dim) || batch_heads < 1 || seq_len < 1) return 0;
   const size_t one = (rk_bytes(batch_heads, seq_len) + 255) / 256 * 256;
   return differential ? 2 * one : one;
@@ -414,10 +417,10 @@ int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dty
                  int normalize, void* workspace, size_t workspace_bytes, int* status, void* stream) {
   if (dtype == TDA_F32) {
     if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
-    if (head_dim == 64 && workspace && batch_heads >= 1 && seq_len >= 1 &&
-        workspace_bytes >= tf32_bytes(batch_heads, seq_len, false))
-      return run_tf32(q, nullptr, k, nullptr, v, out, batch_heads, seq_len, beta, 0.0f, relu_power, normalize,
-                      workspace, status, stream, false);
+    if (tf32_supported(head_dim) && workspace && batch_heads >= 1 && seq_len >= 1 &&
+        workspace_bytes >= tf32_bytes(batch_heads, seq_len, head_dim, false))
+      return run_tf32(q, nullptr, k, nullptr, v, out, batch_heads, seq_len, head_dim, beta, 0.0f, relu_power,
+                      normalize, workspace, status, stream, false);
     return run_simt(q, nullptr, k, nullptr, v, out, batch_heads, seq_len, head_dim, beta, 0.0f, relu_power,
                     normalize, status, stream, false);
   }
@@ -443,10 +446,10 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                  int* status, void* stream) {
   if (dtype == TDA_F32) {
     if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
-    if (head_dim == 64 && workspace && batch_heads >= 1 && seq_len >= 1 &&
-        workspace_bytes >= tf32_bytes(batch_heads, seq_len, true))
-      return run_tf32(q1, q2, k1, k2, v, out, batch_heads, seq_len, beta, clamp01(lambda_param), relu_power,
-                      normalize, workspace, status, stream, true);
+    if (tf32_supported(head_dim) && workspace && batch_heads >= 1 && seq_len >= 1 &&
+        workspace_bytes >= tf32_bytes(batch_heads, seq_len, head_dim, true))
+      return run_tf32(q1, q2, k1, k2, v, out, batch_heads, seq_len, head_dim, beta, clamp01(lambda_param),
+                      relu_power, normalize, workspace, status, stream, true);
     return run_simt(q1, q2, k1, k2, v, out, batch_heads, seq_len, head_dim, beta, clamp01(lambda_param),
                     relu_power, normalize, status, stream, true);
   }

@@ -82,14 +82,14 @@ struct SimtFwdParams {
 
 cudaError_t launch_simt_fwd(const SimtFwdParams& p, int head_dim, cudaStream_t stream);
 
-// Tensor-core fp32 forward at head_dim 64 (tcgen05 kind::tf32, three TF32
-// products per fp32 product).  Sequence padded to whole 64-key tiles.
+// Tensor-core fp32 forward at head_dim 64 / 128 (tcgen05 kind::tf32, three
+// TF32 products per fp32 product).  Sequence padded to whole 64-key tiles.
 inline int64_t tf32_padded_seq(int64_t S) { return (S + 63) / 64 * 64; }
 
 // Caller workspace of the fp32 tensor-core path, per branch: TF32 high / low
-// copies of q and k ([BH][S][64]), the query coefficients 1/m and tau*m and
+// copies of q and k ([BH][S][D]), the query coefficients 1/m and tau*m and
 // the key coefficients 1/m ([BH][S_pad]); shared: V^T high / low copies
-// ([BH][64][S_pad]).  Each array starts on a 256-byte boundary.  With base =
+// ([BH][D][S_pad]).  Each array starts on a 256-byte boundary.  With base =
 // nullptr only `bytes` is computed.
 struct Tf32Workspace {
   float* qh[2];
@@ -104,7 +104,7 @@ struct Tf32Workspace {
   size_t bytes;
 };
 
-inline Tf32Workspace tf32_carve(void* base, int64_t BH, int64_t S, int n_br) {
+inline Tf32Workspace tf32_carve(void* base, int64_t BH, int64_t S, int64_t D, int n_br) {
   Tf32Workspace w{};
   char* b = static_cast<char*>(base);
   size_t off = 0;
@@ -113,7 +113,7 @@ inline Tf32Workspace tf32_carve(void* base, int64_t BH, int64_t S, int n_br) {
     off += (floats * sizeof(float) + 255) / 256 * 256;
     return p;
   };
-  const size_t x = static_cast<size_t>(BH) * S * 64, r = static_cast<size_t>(BH) * tf32_padded_seq(S);
+  const size_t x = static_cast<size_t>(BH) * S * D, r = static_cast<size_t>(BH) * tf32_padded_seq(S);
   for (int br = 0; br < n_br; ++br) {
     w.qh[br] = take(x);
     w.ql[br] = take(x);
@@ -123,14 +123,16 @@ inline Tf32Workspace tf32_carve(void* base, int64_t BH, int64_t S, int n_br) {
     w.tq[br] = take(r);
     w.rk[br] = take(r);
   }
-  w.vth = take(r * 64);
-  w.vtl = take(r * 64);
+  w.vth = take(r * D);
+  w.vtl = take(r * D);
   w.bytes = off;
   return w;
 }
 
-// Tensor maps: q/k high and low copies as 3-D {64, S, BH}, V^T copies as
-// {S_pad, 64, BH}; all fp32 with a {32, 64, 1} box and 128-byte swizzle.
+// Tensor maps, all fp32 with 128-byte swizzle and 32-element (128 B) boxes:
+// q high / low copies as 3-D {D, S, BH} with 64-row boxes, k copies with
+// key-tile-row boxes (tf32_key_tile), V^T copies as {S_pad, D, BH} with D-row
+// boxes.
 struct Tf32FwdParams {
   CUtensorMap tm_qh[2];
   CUtensorMap tm_ql[2];
@@ -141,13 +143,13 @@ struct Tf32FwdParams {
   const float* rq[2];
   const float* tq[2];
   const float* rk[2];
-  float* out;  // [BH][S][64] fp32
+  float* out;  // [BH][S][D] fp32
   int* status;
   int S;
   int S_pad;
   int BH;
   int n_qt;       // 128-row query tiles
-  int n_kt_all;   // 64-key tiles
+  int n_kt_all;   // key tiles (S_pad / tf32_key_tile)
   int causal_skip;
   int n_br;       // 1 rectified, 2 differential
   float relu_power;
@@ -156,10 +158,11 @@ struct Tf32FwdParams {
   int inject;     // test hook: bit 0 = producer never loads Q (forces a timeout)
 };
 
+int tf32_key_tile(int head_dim);  // keys per tile: 64 at head_dim 64, 32 at 128
 cudaError_t launch_tf32_split(const float* const q[2], const float* const k[2], const float* v,
-                              const Tf32Workspace& ws, int n_br, int BH, int S, float beta, int normalize,
+                              const Tf32Workspace& ws, int n_br, int BH, int S, int D, float beta, int normalize,
                               cudaStream_t stream);
-cudaError_t launch_tf32_fwd(const Tf32FwdParams& p, int pow_mode, cudaStream_t stream);
+cudaError_t launch_tf32_fwd(const Tf32FwdParams& p, int head_dim, int pow_mode, cudaStream_t stream);
 
 // CUDA-core fp32 backward of one rectified branch (dq, dk through F.normalize
 // when normalize; dv written or accumulated).  Inputs bf16 or fp32.

@@ -1,6 +1,6 @@
-"""fp32 inputs at head_dim 64 on the tensor cores (three TF32 products per
-fp32 product), through the C ABI: given the workspace that
-``tda_workspace_size(.., TDA_F32, .., 64, ..)`` reports, ``tda_rect_fwd`` /
+"""fp32 inputs at head_dim 64 and 128 on the tensor cores (three TF32 products
+per fp32 product), through the C ABI: given the workspace that
+``tda_workspace_size(.., TDA_F32, .., D, ..)`` reports, ``tda_rect_fwd`` /
 ``tda_diff_fwd`` take that path; without a workspace they run the exact-fp32
 CUDA-core kernel.  Both are checked against the fp64 oracle at the fp32
 tolerance (rel-L2 <= 1e-5) and against each other, on ragged lengths,
@@ -19,30 +19,38 @@ DEV = "cuda"
 TOL_F32 = 1e-5
 
 CASES = [
-    # (batch_heads, S, beta, p, normalize, differential)
-    (2, 1, 1.0, 2.0, True, False),
-    (2, 63, 1.0, 2.0, True, True),
-    (3, 200, -0.5, 2.0, True, False),
-    (1, 129, 0.0, 1.0, False, True),
-    (2, 300, 1.0, 1.5, False, False),
-    (1, 1000, 0.5, 3.0, True, True),
-    (4, 256, 2.0, 2.0, True, True),
-    (1, 777, -1.0, 1.0, True, True),
+    # (batch_heads, S, beta, p, normalize, differential, head_dim)
+    (2, 1, 1.0, 2.0, True, False, 64),
+    (2, 63, 1.0, 2.0, True, True, 64),
+    (3, 200, -0.5, 2.0, True, False, 64),
+    (1, 129, 0.0, 1.0, False, True, 64),
+    (2, 300, 1.0, 1.5, False, False, 64),
+    (1, 1000, 0.5, 3.0, True, True, 64),
+    (4, 256, 2.0, 2.0, True, True, 64),
+    (1, 777, -1.0, 1.0, True, True, 64),
+    (2, 1, 1.0, 2.0, True, False, 128),
+    (2, 95, 1.0, 2.0, True, True, 128),
+    (3, 200, -0.5, 2.0, True, False, 128),
+    (1, 129, 0.0, 1.0, False, True, 128),
+    (2, 300, 1.0, 1.5, False, False, 128),
+    (1, 1000, 0.5, 3.0, True, True, 128),
+    (1, 777, -1.0, 1.0, True, True, 128),
 ]
 
 
 def _run(lib, xs, BH, S, beta, lam, p, normalize, diff, with_ws):
-    out = torch.empty((BH, S, 64), dtype=torch.float32, device=DEV)
+    D = xs[0].shape[-1]
+    out = torch.empty((BH, S, D), dtype=torch.float32, device=DEV)
     status = ops._status_word(torch.device(DEV))
-    ws_n = lib.tda_workspace_size(int(diff), _lib.TDA_F32, BH, S, 64, int(normalize)) if with_ws else 0
+    ws_n = lib.tda_workspace_size(int(diff), _lib.TDA_F32, BH, S, D, int(normalize)) if with_ws else 0
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=DEV)
     st = torch.cuda.current_stream().cuda_stream
     ptr = [x.data_ptr() for x in xs]
     if diff:
-        rc = lib.tda_diff_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, BH, S, 64, beta, lam, p,
+        rc = lib.tda_diff_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, BH, S, D, beta, lam, p,
                               int(normalize), ws.data_ptr() if ws_n else None, ws_n, status.data_ptr(), st)
     else:
-        rc = lib.tda_rect_fwd(ptr[0], ptr[2], ptr[4], out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, BH, S, 64, beta,
+        rc = lib.tda_rect_fwd(ptr[0], ptr[2], ptr[4], out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, BH, S, D, beta,
                               p, int(normalize), ws.data_ptr() if ws_n else None, ws_n, status.data_ptr(), st)
     _lib.check(rc)
     torch.cuda.synchronize()
@@ -57,16 +65,17 @@ def test_workspace_size_reports_the_split_copies():
     diff = lib.tda_workspace_size(1, _lib.TDA_F32, BH, S, 64, 0)
     # at least the high / low copies of q, k (per branch) and of v
     assert rect >= 6 * BH * S * 64 * 4 and diff >= 10 * BH * S * 64 * 4
-    assert lib.tda_workspace_size(0, _lib.TDA_F32, BH, S, 128, 1) == 0  # CUDA-core path, no workspace
+    assert lib.tda_workspace_size(0, _lib.TDA_F32, BH, S, 128, 1) >= 6 * BH * S * 128 * 4
+    assert lib.tda_workspace_size(0, _lib.TDA_F32, BH, S, 32, 1) == 0  # CUDA-core path, no workspace
 
 
-@pytest.mark.parametrize("case", CASES, ids=[f"bh{c[0]}_S{c[1]}_b{c[2]}_p{c[3]}_n{int(c[4])}_d{int(c[5])}"
+@pytest.mark.parametrize("case", CASES, ids=[f"bh{c[0]}_S{c[1]}_b{c[2]}_p{c[3]}_n{int(c[4])}_d{int(c[5])}_D{c[6]}"
                                              for c in CASES])
 def test_tensor_core_fp32_matches_oracle_and_cuda_core(case):
-    BH, S, beta, p, normalize, diff = case
+    BH, S, beta, p, normalize, diff, D = case
     lam = 0.6
-    g = torch.Generator().manual_seed(BH * 1000 + S)
-    xs_h = [torch.randn((BH, S, 64), generator=g) * (1.0 if normalize else 2.0) for _ in range(5)]
+    g = torch.Generator().manual_seed(BH * 1000 + S + D)
+    xs_h = [torch.randn((BH, S, D), generator=g) * (1.0 if normalize else 2.0) for _ in range(5)]
     xs = [x.to(DEV) for x in xs_h]
     xn = [x.numpy()[None] for x in xs_h]
     if diff:
@@ -120,13 +129,14 @@ def test_timeout_reports_status_and_context_survives():
     assert O.rel_l2(out, ref) <= TOL_F32
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("beta", [1.0, -0.5])
-def test_long_sequence_sampled_rows(beta):
-    """S = 4096 (64 key tiles accumulated per row): a sample of query rows at
-    the start, middle and end against the oracle, differential form."""
+def test_long_sequence_sampled_rows(beta, D):
+    """S = 4096 (64 or 128 key tiles accumulated per row): a sample of query
+    rows at the start, middle and end against the oracle, differential form."""
     BH, S = 2, 4096
-    g = torch.Generator().manual_seed(4096 + int(10 * beta))
-    xs_h = [torch.randn((BH, S, 64), generator=g) for _ in range(5)]
+    g = torch.Generator().manual_seed(4096 + int(10 * beta) + D)
+    xs_h = [torch.randn((BH, S, D), generator=g) for _ in range(5)]
     xs = [x.to(DEV) for x in xs_h]
     rows = list(range(0, 64)) + list(range(2000, 2064)) + list(range(S - 64, S))
     lib = _lib.load()

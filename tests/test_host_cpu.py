@@ -48,7 +48,9 @@ def test_library_host_only_calls():
     # per-row coefficient arrays (1024 B each, seq padded to 128) and V^T high / low (65536 B each)
     assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 64, 1) == 4 * 51200 + 3 * 1024 + 2 * 65536
     assert lib.tda_workspace_size(1, _lib.TDA_F32, 2, 100, 64, 0) == 8 * 51200 + 6 * 1024 + 2 * 65536
-    assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 128, 1) == 0
+    # head_dim 128: copies of 2 x 100 x 128 floats (102400 B), V^T copies of 2 x 128 x 128 (131072 B)
+    assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 128, 1) == 4 * 102400 + 3 * 1024 + 2 * 131072
+    assert lib.tda_workspace_size(0, _lib.TDA_F32, 2, 100, 32, 1) == 0
 
 
 def test_library_rejects_bad_arguments_without_launching():
