@@ -34,9 +34,9 @@
  *     tda_last_error() (thread-local).
  *
  * Supported: dtype TDA_BF16 with head_dim 64 or 128 runs on the tcgen05
- * tensor cores; dtype TDA_F32 with head_dim 64, given the workspace that
- * tda_workspace_size reports, runs on the tcgen05 tensor cores too (three
- * TF32 products per fp32 product, fp32 accuracy); dtype TDA_F32 with
+ * tensor cores; dtype TDA_F32 with head_dim 64 or 128, given the workspace
+ * that tda_workspace_size reports, runs on the tcgen05 tensor cores too
+ * (three TF32 products per fp32 product, fp32 accuracy); dtype TDA_F32 with
  * head_dim in {16, 32, 64, 128, 256} and no workspace runs the exact-fp32
  * CUDA-core kernel.  Other combinations return TDA_ERR_UNSUPPORTED (the
  * Python layer widens them to fp32 first).
@@ -70,8 +70,8 @@ const char* tda_last_error(void);
  * tda_diff_fwd (differential = 1) for these sizes.  Replaces the fp32 upcast
  * copies the reference allocates per call (triton_threshold_attention.py:356-363):
  * for bf16 only per-key inverse norms (normalize) are kept; for fp32 at
- * head_dim 64 it holds the TF32 high / low copies of q, k and v^T and per-row
- * coefficients of the tensor-core path (about 2.5x the input bytes);
+ * head_dim 64 or 128 it holds the TF32 high / low copies of q, k and v^T and
+ * per-row coefficients of the tensor-core path (about 2.5x the input bytes);
  * other fp32 head dims need none. */
 size_t tda_workspace_size(int differential, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim,
                           int normalize);
