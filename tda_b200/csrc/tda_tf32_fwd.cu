@@ -1,4 +1,4 @@
-// Tensor-core forward for fp32 inputs at head_dim 64 (tcgen05, kind::tf32).
+// Tensor-core forward for fp32 inputs at head_dim 64 and 128 (tcgen05, kind::tf32).
 //
 // fp32 results must stay within 1e-5 rel-L2 of an fp64 oracle; one TF32
 // product per score (10-bit mantissa) misses that by far.  Each fp32 operand
@@ -14,11 +14,12 @@
 // branches accumulate into one output, the second weighted by -clamp(lambda)).
 //
 // Pre-pass (one stream-ordered launch, into the caller's workspace):
-//   q, k rows -> h, l copies [BH][S][64], and per row 1/m, tau*m (queries) or
+//   q, k rows -> h, l copies [BH][S][D], and per row 1/m, tau*m (queries) or
 //   1/m (keys), m = max(||x||, 1e-12) when normalized, m = 1 otherwise;
-//   v -> transposed h, l copies [BH][64][S_pad] (zero past S), so that V^T is
+//   v -> transposed h, l copies [BH][D][S_pad] (zero past S), so that V^T is
 //   a K-major operand like K.
-// Main kernel: one CTA = 128 query rows of one (batch, head); 64-key tiles.
+// Main kernel: one CTA = 128 query rows of one (batch, head); key tiles of 64
+// (head_dim 64) or 32 (head_dim 128); layout per head_dim in TfCfg below.  At 64:
 //   warp 0  TMA producer: Q h/l once per branch, K h/l and V^T h/l rings of
 //           two entries each (K released by QK, V by PV)
 //   warp 1  MMA issuer (one thread): S = Q K^T (3 x 8 MMAs of M128 N64 K8)
