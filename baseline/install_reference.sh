@@ -7,10 +7,15 @@
 # directory as it is.  The source is copied to a scratch directory (the
 # reference tree is read-only) and given packaging metadata only: a
 # pyproject.toml naming the one module.  The module itself is not changed.
-# Run in the build container, where the reference is mounted; baseline/_ref is
-# git-ignored and travels with the repository snapshot to the GPU box.
+# Usage: baseline/install_reference.sh <path of the reference checkout>
+# Run where the reference is available; baseline/_ref is git-ignored and
+# travels with the repository snapshot to the GPU box.
 set -euo pipefail
-REF=${1:-/root/reference}
+if [ $# -ne 1 ]; then
+  echo "usage: $0 <path of the reference checkout (the directory holding triton_threshold_attention.py)>" >&2
+  exit 2
+fi
+REF=$1
 HERE=$(cd "$(dirname "$0")" && pwd)
 TMP=$(mktemp -d)
 trap 'rm -rf "$TMP"' EXIT

@@ -27,7 +27,15 @@
  *     asynchronous and stream-ordered; no host synchronisation happens.
  *   - status points to one device int32 that the kernels set to a nonzero
  *     code when a bounded internal wait gives up (the output is then
- *     invalid).  It is never cleared by the library.
+ *     invalid).  It is never cleared by the library.  A kernel reacts only to
+ *     a change of the word during its own run, so a code left by an earlier
+ *     call does not stop later calls.
+ *   - Persistent kernel: at head_dim 128 with seq_len <= 4096 the rectified
+ *     form runs a one-CTA-per-SM kernel that takes query tiles from a work
+ *     counter in the library (1024 words, used round-robin).  At most 1024
+ *     such launches of one process may be in flight at the same time, across
+ *     all streams and CUDA graphs (a graph that captured a launch keeps its
+ *     word); a 1025th concurrent launch would share a word with a running one.
  *   - workspace is device scratch of at least tda_workspace_size() bytes
  *     (may be NULL when that size is 0).  It is only used during the call.
  *   - Return value: TDA_OK, or a negative TDA_ERR_* code with a message from
@@ -95,6 +103,25 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
                  int dtype, int out_dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta,
                  float lambda_param, float relu_power, int normalize, void* workspace, size_t workspace_bytes,
                  int* status, void* stream);
+
+/* tda_diff_fwd with lambda as a device tensor instead of a host scalar:
+ * out[b][h] = rect(q1, k1, v)[b][h] - clamp(lambda[b * lambda_stride_batch +
+ * h * lambda_stride_head], 0, 1) * rect(q2, k2, v)[b][h], computed in the same
+ * single fused pass.  Replaces the reference's combine with a tensor lambda
+ * that broadcasts over (batch, head) -- a scalar, a per-head or a
+ * per-(batch, head) weight (triton_threshold_attention.py:516-517) -- without
+ * a second kernel pass and without reading lambda on the host (no host
+ * synchronisation).  lambda points to fp32 values on the device; a stride of 0
+ * broadcasts that dimension (both 0: one scalar).  Inputs are (batch, heads,
+ * seq_len, head_dim): contiguous when strides is NULL (any dtype / head_dim
+ * tda_diff_fwd accepts, same workspace), or bf16 strided views at head_dim 64 /
+ * 128 as for tda_diff_fwd_strided (15 element strides).  out is a contiguous
+ * (batch * heads, seq_len, head_dim) array. */
+int tda_diff_fwd_lambda(const void* q1, const void* q2, const void* k1, const void* k2, const void* v,
+                        const int64_t* strides, void* out, int dtype, int out_dtype, int64_t batch, int64_t heads,
+                        int64_t seq_len, int64_t head_dim, float beta, const float* lambda_param,
+                        int64_t lambda_stride_batch, int64_t lambda_stride_head, float relu_power, int normalize,
+                        void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 /* Device workspace bytes needed by tda_rect_bwd for these sizes (0 on the
  * CUDA-core path): the key table of k (normalize) and a per-query table of
@@ -180,6 +207,9 @@ int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* 
  * The scratch (inverse key norms) lives in a fixed 8.5 MiB array inside the
  * library, reserved on every GPU that loads it: requires
  * batch_heads * round_up(seq_len, 128) <= 1048576, else TDA_ERR_INVALID.
+ * fp32 inputs run the exact-fp32 CUDA-core kernel here (the tensor-core fp32
+ * path of tda_diff_fwd needs a caller workspace), and calls with
+ * normalize = 0 need no scratch at all.
  * Makes no cudaMalloc / cudaFree call.  The first call on a device looks up
  * the array's address (do it before any stream capture).  All calls share the
  * array: calls whose GPU work overlaps race and must be ordered on one stream. */

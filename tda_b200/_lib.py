@@ -40,6 +40,8 @@ SIGNATURES = {
     "tda_rect_fwd_strided": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _F, _F, _I, _P, _SZ, _P, _P]),
     "tda_diff_fwd_strided": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _F, _F, _F, _I, _P, _SZ,
                                   _P, _P]),
+    "tda_diff_fwd_lambda": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _I64, _F, _P, _I64, _I64, _F,
+                                 _I, _P, _SZ, _P, _P]),
     "tda_bwd_workspace_size": (_SZ, [_I, _I64, _I64, _I64, _I]),
     "tda_rect_bwd": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64, _F, _F, _I, _F, _I, _P, _SZ, _P, _P]),
 }

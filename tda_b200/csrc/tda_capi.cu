@@ -140,9 +140,13 @@ int check_common(int64_t BH, int64_t S, int64_t D, int* status) {
 
 bool tc_supported(int dtype, int64_t D) { return dtype == TDA_BF16 && (D == 64 || D == 128); }
 
+// No device lambda: every (batch, head) uses the host scalar.
+constexpr tda::LamSpec kNoLam{nullptr, 0, 0, 1};
+
 int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const View& v, void* out, int out_dtype,
            int64_t BH, int64_t heads, int64_t S, int64_t D, float beta, float lam, float p, int normalize,
-           const float* rk1, const float* rk2, int* status, void* stream, bool differential) {
+           const float* rk1, const float* rk2, int* status, void* stream, bool differential,
+           const tda::LamSpec& lam_dev = kNoLam) {
   if (int e = check_common(BH, S, D, status)) return e;
   if (heads < 1 || BH % heads != 0) return fail(TDA_ERR_INVALID, "heads must divide batch * heads");
   if (!(D == 64 || D == 128)) return fail(TDA_ERR_UNSUPPORTED, "tensor-core path needs head_dim 64 or 128");
@@ -185,6 +189,7 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
   prm.relu_power = p;
   prm.lam = lam;
   prm.lam_root = p == 2.0f ? std::sqrt(lam) : (p == 3.0f ? std::cbrt(lam) : lam);
+  prm.lam_dev = lam_dev;
   prm.tau_scale = 2.0f / static_cast<float>(D);
   prm.timeout_ns = g_timeout_ns.load();
   prm.inject = g_inject.load();
@@ -199,7 +204,7 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
 
 int run_simt(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int64_t BH,
              int64_t S, int64_t D, float beta, float lam, float p, int normalize, int* status, void* stream,
-             bool differential) {
+             bool differential, const tda::LamSpec& lam_dev = kNoLam) {
   if (int e = check_common(BH, S, D, status)) return e;
   const void* ins[5] = {q1, k1, v, differential ? q2 : q1, differential ? k2 : k1};
   for (const void* x : ins)
@@ -217,6 +222,7 @@ int run_simt(const void* q1, const void* q2, const void* k1, const void* k2, con
   prm.beta = beta;
   prm.relu_power = p;
   prm.lam = lam;
+  prm.lam_dev = lam_dev;
   prm.normalize = normalize != 0;
   prm.differential = differential;
   cudaError_t ce = tda::launch_simt_fwd(prm, static_cast<int>(D), static_cast<cudaStream_t>(stream));
@@ -234,7 +240,7 @@ size_t tf32_bytes(int64_t BH, int64_t S, int64_t D, bool differential) {
 
 int run_tf32(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int64_t BH,
              int64_t S, int64_t D, float beta, float lam, float p, int normalize, void* workspace, int* status,
-             void* stream, bool differential) {
+             void* stream, bool differential, const tda::LamSpec& lam_dev = kNoLam) {
   if (int e = check_common(BH, S, D, status)) return e;
   const void* ins[5] = {q1, k1, v, differential ? q2 : q1, differential ? k2 : k1};
   for (const void* x : ins)
@@ -277,6 +283,7 @@ int run_tf32(const void* q1, const void* q2, const void* k1, const void* k2, con
   prm.n_br = n_br;
   prm.relu_power = p;
   prm.lam = lam;
+  prm.lam_dev = lam_dev;
   prm.timeout_ns = g_timeout_ns.load();
   prm.inject = g_inject.load();
   ce = tda::launch_tf32_fwd(prm, static_cast<int>(D), tda::pow_mode_of(p), st);
@@ -294,7 +301,7 @@ void tda::set_last_error(const char* msg) { g_last_error = msg ? msg : ""; }
 
 extern "C" {
 
-int tda_version(void) { return 100; }
+int tda_version(void) { return 101; }
 
 const char* tda_last_error(void) { return g_last_error.c_str(); }
 
@@ -346,7 +353,7 @@ namespace {
 // Strided entry points: key tables of the strided keys, then the fused kernel.
 int run_strided(const View* views, int n, void* out, int out_dtype, int64_t batch, int64_t heads, int64_t S,
                 int64_t D, float beta, float lam, float p, int normalize, void* workspace, size_t workspace_bytes,
-                int* status, void* stream) {
+                int* status, void* stream, const tda::LamSpec& lam_dev = kNoLam) {
   const bool diff = n == 5;
   if (batch < 1 || heads < 1) return fail(TDA_ERR_INVALID, "batch and heads must be >= 1");
   if (!(D == 64 || D == 128))
@@ -382,7 +389,7 @@ int run_strided(const View* views, int n, void* out, int out_dtype, int64_t batc
     if (ce != cudaSuccess) return cuda_fail(ce, "key table launch");
   }
   return run_tc(q1, q2, k1, k2, v, out, out_dtype, BH, heads, S, D, beta, lam, p, normalize, rk1, rk2, status, stream,
-                diff);
+                diff, lam_dev);
 }
 }  // namespace
 
@@ -559,6 +566,57 @@ int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, 
   cudaError_t ce = tda::launch_rect_bwd(prm, static_cast<int>(head_dim), dtype == TDA_BF16, st);
   if (ce != cudaSuccess) return cuda_fail(ce, "backward kernel launch");
   return TDA_OK;
+}
+
+int tda_diff_fwd_lambda(const void* q1, const void* q2, const void* k1, const void* k2, const void* v,
+                        const int64_t* strides, void* out, int dtype, int out_dtype, int64_t batch, int64_t heads,
+                        int64_t seq_len, int64_t head_dim, float beta, const float* lambda_param,
+                        int64_t lambda_stride_batch, int64_t lambda_stride_head, float relu_power, int normalize,
+                        void* workspace, size_t workspace_bytes, int* status, void* stream) {
+  if (batch < 1 || heads < 1) return fail(TDA_ERR_INVALID, "batch and heads must be >= 1");
+  if (!lambda_param || (reinterpret_cast<uintptr_t>(lambda_param) & 3u))
+    return fail(TDA_ERR_INVALID, "lambda must be a non-NULL, 4-byte aligned device pointer to fp32 values");
+  if (lambda_stride_batch < 0 || lambda_stride_head < 0)
+    return fail(TDA_ERR_INVALID, "lambda strides must be >= 0");
+  if (heads > 0x7fffffffll) return fail(TDA_ERR_INVALID, "heads too large");
+  const tda::LamSpec lam{lambda_param, static_cast<long long>(lambda_stride_batch),
+                         static_cast<long long>(lambda_stride_head), static_cast<int>(heads)};
+  const int64_t BH = batch * heads;
+  if (strides) {
+    if (dtype != TDA_BF16) return fail(TDA_ERR_UNSUPPORTED, "strided inputs must be bf16");
+    const View views[5] = {{q1, strides[0], strides[1], strides[2]},
+                           {q2, strides[3], strides[4], strides[5]},
+                           {k1, strides[6], strides[7], strides[8]},
+                           {k2, strides[9], strides[10], strides[11]},
+                           {v, strides[12], strides[13], strides[14]}};
+    return run_strided(views, 5, out, out_dtype, batch, heads, seq_len, head_dim, beta, 0.0f, relu_power, normalize,
+                       workspace, workspace_bytes, status, stream, lam);
+  }
+  if (dtype == TDA_F32) {
+    if (out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "fp32 inputs produce fp32 output");
+    if (tf32_supported(head_dim) && workspace && workspace_bytes >= tf32_bytes(BH, seq_len, head_dim, true))
+      return run_tf32(q1, q2, k1, k2, v, out, BH, seq_len, head_dim, beta, 0.0f, relu_power, normalize, workspace,
+                      status, stream, true, lam);
+    return run_simt(q1, q2, k1, k2, v, out, BH, seq_len, head_dim, beta, 0.0f, relu_power, normalize, status, stream,
+                    true, lam);
+  }
+  if (dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
+  if (!tc_supported(dtype, head_dim))
+    return fail(TDA_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
+                static_cast<long long>(head_dim));
+  float* rk1 = nullptr;
+  float* rk2 = nullptr;
+  if (normalize) {
+    const size_t need = tda_workspace_size(1, dtype, BH, seq_len, head_dim, normalize);
+    if (!workspace || workspace_bytes < need) return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+    rk1 = static_cast<float*>(workspace);
+    rk2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2);
+    if (int e = tda_key_inv_norms(k1, dtype, BH, seq_len, head_dim, rk1, stream)) return e;
+    if (int e = tda_key_inv_norms(k2, dtype, BH, seq_len, head_dim, rk2, stream)) return e;
+  }
+  auto cv = [&](const void* x) { return contiguous_view(x, BH, seq_len, head_dim); };
+  return run_tc(cv(q1), cv(q2), cv(k1), cv(k2), cv(v), out, out_dtype, BH, BH, seq_len, head_dim, beta, 0.0f,
+                relu_power, normalize, rk1, rk2, status, stream, true, lam);
 }
 
 }  // extern "C"

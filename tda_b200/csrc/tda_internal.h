@@ -19,6 +19,25 @@ inline int pow_mode_of(float p) {
   return POW_GENERAL;
 }
 
+// lambda of the differential form read on the device per (batch, head): the
+// weight of the second branch is clamp(ptr[b * sb + h * sh], 0, 1) with
+// b = bh / heads, h = bh % heads (sb / sh = 0 broadcast that dimension).
+// ptr == nullptr: every (batch, head) uses the host scalar instead.
+struct LamSpec {
+  const float* ptr;
+  long long sb;
+  long long sh;
+  int heads;
+};
+
+#ifdef __CUDACC__
+__device__ __forceinline__ float lambda_of(const LamSpec& l, int bh, float scalar) {
+  if (l.ptr == nullptr) return scalar;
+  const float x = __ldg(l.ptr + (bh / l.heads) * l.sb + (bh % l.heads) * l.sh);
+  return fminf(fmaxf(x, 0.0f), 1.0f);
+}
+#endif
+
 // Query/key tile edge of the tensor-core kernels (one UMMA M / one key block).
 constexpr int kTile = 128;
 
@@ -53,6 +72,7 @@ struct TcFwdParams {
   float relu_power;
   float lam;          // clamped lambda (differential)
   float lam_root;     // lambda^(1/p) for p in {1, 2, 3} (folded into the second branch)
+  LamSpec lam_dev;    // per-(batch, head) lambda on the device (ptr null: lam / lam_root)
   float tau_scale;    // 2 / D
   unsigned long long timeout_ns;
   int inject;         // test hook: bit 0 = producer never loads Q (forces a timeout)
@@ -76,6 +96,7 @@ struct SimtFwdParams {
   float beta;
   float relu_power;
   float lam;
+  LamSpec lam_dev;  // per-(batch, head) lambda on the device (ptr null: lam)
   int normalize;
   int differential;
 };
@@ -154,6 +175,7 @@ struct Tf32FwdParams {
   int n_br;       // 1 rectified, 2 differential
   float relu_power;
   float lam;      // clamped lambda (second branch weight -lam)
+  LamSpec lam_dev;  // per-(batch, head) lambda on the device (ptr null: lam)
   unsigned long long timeout_ns;
   int inject;     // test hook: bit 0 = producer never loads Q (forces a timeout)
 };

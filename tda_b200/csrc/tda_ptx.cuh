@@ -57,11 +57,20 @@ struct WaitCtl {
   volatile int* abort_flag;  // in shared memory
   int* status;               // device status word (global)
   uint64_t timeout_ns;
+  int status0;               // the status word as this thread saw it at start-up
 };
+
+// The status word is sticky (only the caller clears it), so a code left by an
+// earlier launch must not stop this one: each thread records the word's value
+// when its CTA starts and later reacts only to a change.
+__device__ __forceinline__ WaitCtl make_wait_ctl(volatile int* abort_flag, int* status, uint64_t timeout_ns) {
+  return WaitCtl{abort_flag, status, timeout_ns, *reinterpret_cast<volatile int*>(status)};
+}
 
 // After 1 ms of waiting the status word is polled as well, so once one CTA of
 // a grid has given up the others stop within about a millisecond instead of
-// each running out its own timeout.
+// each running out its own timeout.  Only a change of the word since this
+// CTA started counts (see make_wait_ctl).
 static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, const WaitCtl& ctl, int code) {
   const uint64_t t0 = global_timer_ns();
   uint32_t it = 0;
@@ -70,7 +79,7 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
     if ((++it & 31u) == 0) {
       if (*ctl.abort_flag) return false;
       const uint64_t waited = global_timer_ns() - t0;
-      if (waited > 1000000ull && *reinterpret_cast<volatile int*>(ctl.status) != 0) {
+      if (waited > 1000000ull && *reinterpret_cast<volatile int*>(ctl.status) != ctl.status0) {
         *ctl.abort_flag = 1;
         return false;
       }

@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kSimtThreads) tda_simt_fwd_kernel(const SimtFw
   for (int br = 0; br < n_branch; ++br) {
     const float* q = br ? p.q2 : p.q1;
     const float* k = br ? p.k2 : p.k1;
-    const float w = br ? -p.lam : 1.0f;
+    const float w = br ? -lambda_of(p.lam_dev, bh, p.lam) : 1.0f;
     __syncthreads();  // the previous branch's last tile fully consumed
     load_rows<D>(Qs, C::LD, q, bh, m0, p.S);
     load_rows_async<D>(stage0, C::LD, k, bh, 0, p.S);

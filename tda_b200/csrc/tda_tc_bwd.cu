@@ -534,7 +534,7 @@ __global__ void __maxnreg__(168) tda_tc_bwd_dq_kernel(const __grid_constant__ Tc
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const WaitCtl ctl{&bars->abort_flag, p.status, p.timeout_ns};
+  const WaitCtl ctl = make_wait_ctl(&bars->abort_flag, p.status, p.timeout_ns);
   if (warp == 0) {
     if (lane == 0) dq_producer<D, NORM>(p, smem, bars, ctl, bh, qt, n_kt);
     __syncwarp();
@@ -875,7 +875,7 @@ __global__ void __maxnreg__(168) tda_tc_bwd_dkv_kernel(const __grid_constant__ T
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const WaitCtl ctl{&bars->abort_flag, p.status, p.timeout_ns};
+  const WaitCtl ctl = make_wait_ctl(&bars->abort_flag, p.status, p.timeout_ns);
   if (warp == 0) {
     if (lane == 0) dkv_producer<D>(p, smem, bars, ctl, bh, kt, i0, n_steps);
     __syncwarp();

@@ -432,8 +432,13 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
 
   // tau(i) = beta * sqrt(2 * log(i + 1) / D) in fp32 (triton_threshold_attention.py:62-63)
   const float tau = p.beta * sqrtf((2.0f * logf(static_cast<float>(grow + 1))) / static_cast<float>(D));
-  const float lam2 = (DIFF && kFold) ? p.lam_root : 1.0f;
-  RowCoef c{tau, 1.0f, tau, lam2};
+  float lam = p.lam, lam_root = p.lam_root;
+  if (DIFF && p.lam_dev.ptr) {  // lambda of this (batch, head) from the device
+    lam = lambda_of(p.lam_dev, bh, p.lam);
+    lam_root = lambda_root<PM>(lam);
+  }
+  const float lam2 = (DIFF && kFold) ? lam_root : 1.0f;
+  RowCoef c{tau, 1.0f, tau, lam2, lam};
   bool ok = true;
   if constexpr (NORM) {
     ok = mbar_wait_warp(&bars->q_full, 0, ctl, ST_TR_Q);
@@ -496,7 +501,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     const uint32_t s1col = C::col_s(slot);
     const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>>(
         tmem + lane_off, s1col, C::kColS2, wg, rk_s + re * C::kRkPerTile, grow - j * kTile, j >= qt, c,
-        p.relu_power, p.lam, [&] {
+        p.relu_power, c.lam, [&] {
           // S2 is in registers: hand its TMEM slot back so QK2 of the next
           // tile runs on the tensor cores while this tile is transformed
           tc_fence_before();
@@ -637,7 +642,7 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const WaitCtl ctl{&bars->abort_flag, p.status, p.timeout_ns};
+  const WaitCtl ctl = make_wait_ctl(&bars->abort_flag, p.status, p.timeout_ns);
 
   if (warp == 0) {
     if (lane == 0) run_producer<D, DIFF, NORM>(p, smem, bars, ctl, bh, qt, n_kt);
@@ -1019,8 +1024,13 @@ __device__ bool p_prologue(const TcFwdParams& p, uint8_t* smem, PBars* bars, con
   if (idx >= 0) decode_item(p, idx, bh, qt);
   const int grow = qt * kTile + row;
   const float tau = p.beta * sqrtf((2.0f * logf(static_cast<float>(grow + 1))) / static_cast<float>(D));
-  const float lam2 = (DIFF && kFold) ? p.lam_root : 1.0f;
-  c = RowCoef{tau, 1.0f, tau, lam2};
+  float lam = p.lam, lam_root = p.lam_root;
+  if (DIFF && p.lam_dev.ptr && idx >= 0) {  // lambda of this item's (batch, head) from the device
+    lam = lambda_of(p.lam_dev, bh, p.lam);
+    lam_root = lambda_root<PM>(lam);
+  }
+  const float lam2 = (DIFF && kFold) ? lam_root : 1.0f;
+  c = RowCoef{tau, 1.0f, tau, lam2, lam};
   bool live = ok && idx >= 0;
   if constexpr (NORM) {
     const int b = DIFF ? 0 : (it & 1);
@@ -1103,7 +1113,7 @@ __device__ void p_transform(const TcFwdParams& p, uint8_t* smem, PBars* bars, co
     tc_fence_after();
     const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>>(
         tmem + lane_off, C::col_s(slot), C::kColS2, wg, rk_s + re * C::kRkPerTile, qt * kTile + row - j * kTile,
-        j >= qt, c, p.relu_power, p.lam, [&] {
+        j >= qt, c, p.relu_power, c.lam, [&] {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->s2_free[G & 1]);
@@ -1293,7 +1303,7 @@ __global__ void __maxnreg__(168) tda_tc_fwd_persistent_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const WaitCtl ctl{&bars->abort_flag, p.status, p.timeout_ns};
+  const WaitCtl ctl = make_wait_ctl(&bars->abort_flag, p.status, p.timeout_ns);
   if (warp == 0) {
     if (lane == 0) p_producer<D, DIFF, NORM>(p, smem, bars, ctl, n_items);
     __syncwarp();
@@ -1391,16 +1401,13 @@ cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, cu
 }  // namespace
 
 // Work-item counters of the persistent kernel: one per launch in flight, taken
-// round-robin and zeroed in the launch's stream right before it.
+// round-robin and zeroed in the launch's stream right before it.  Limit: at
+// most 1024 persistent launches of one process may be in flight at once
+// (across all streams and CUDA graphs; a graph that captured a launch keeps
+// its counter word for good).  The 1025th concurrent launch would share a
+// word with a running one, which would then skip work items.
 __device__ unsigned g_item_ctr[1024];
 
-// Kernel choice.  Measured on B200 (bf16, beta = 1): the persistent kernel
-// gains where a query tile has few key tiles, so that per-tile start-up and
-// epilogue are a large share -- rect (4,32,4096,128) +4%, (4,32,2048,128)
-// +6.7% -- is even at S = 8192 (rect), loses 4% at head_dim 64
-// ((2,16,2048,64)) and 3.6% on the differential form, whose single Q1/Q2
-// buffer and unstaged output leave its item boundaries on the critical path.
-// TDA_B200_FWD_PERSISTENT=1 / =0 forces either kernel.
 static bool use_persistent_forward(bool differential, int head_dim, int n_qtiles) {
   static const int forced = [] {
     const char* v = std::getenv("TDA_B200_FWD_PERSISTENT");
@@ -1410,10 +1417,29 @@ static bool use_persistent_forward(bool differential, int head_dim, int n_qtiles
   return !differential && head_dim == 128 && n_qtiles <= 32;
 }
 
+// Device address of g_item_ctr on the current device, looked up once per
+// device (the host-side symbol is only a stand-in for it).
+static cudaError_t item_counters_on_current_device(unsigned** out) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<unsigned*> addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  unsigned* a = addr[dev].load(std::memory_order_acquire);
+  if (!a) {
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&a), g_item_ctr);
+    if (e != cudaSuccess) return e;
+    addr[dev].store(a, std::memory_order_release);
+  }
+  *out = a;
+  return cudaSuccess;
+}
+
 static cudaError_t prepare_item_counter(TcFwdParams& p, cudaStream_t stream) {
   static std::atomic<unsigned> next{0};
   unsigned* base = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&base), g_item_ctr);
+  cudaError_t e = item_counters_on_current_device(&base);
   if (e != cudaSuccess) return e;
   p.item_ctr = base + (next.fetch_add(1u) % 1024u);
   return cudaMemsetAsync(p.item_ctr, 0, sizeof(unsigned), stream);

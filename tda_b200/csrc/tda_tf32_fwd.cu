@@ -431,7 +431,7 @@ __device__ void tf_transform(const Tf32FwdParams& p, Tf32Bars* b, const WaitCtl&
   for (int t = 0; t < T; ++t) {
     const int br = t / n_kt, j = t % n_kt, e = t & 1, u = t >> 1;
     if (j == 0) {
-      w = br ? -p.lam : 1.0f;
+      w = br ? -lambda_of(p.lam_dev, bh, p.lam) : 1.0f;
       rq = gi < p.S ? p.rq[br][rbase + gi] : 0.0f;  // rows past S: z = 0, P = 0
       tq = gi < p.S ? p.tq[br][rbase + gi] : 0.0f;
     }
@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(TfCfg<D>::kThreads, 1) tda_tf32_fwd_kernel(con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = b->tmem_base;
-  const WaitCtl ctl{&b->abort_flag, p.status, p.timeout_ns};
+  const WaitCtl ctl = make_wait_ctl(&b->abort_flag, p.status, p.timeout_ns);
   if (warp == 0) {
     if (lane == 0) tf_producer<D>(p, smem, b, ctl, bh, m0, n_kt);
     __syncwarp();

@@ -34,7 +34,17 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, const
 // lambda multiply.
 struct RowCoef {
   float tq1, rq1, tq2, rq2;
+  float lam;  // clamped lambda of this (batch, head) (the general power's explicit weight)
 };
+
+// lambda^(1/p) for the folded powers (lambda itself for the general one, which
+// weights the second branch explicitly).
+template <int PM>
+__device__ __forceinline__ float lambda_root(float lam) {
+  if constexpr (PM == POW_2) return sqrtf(lam);
+  if constexpr (PM == POW_3) return cbrtf(lam);
+  return lam;
+}
 
 __device__ __forceinline__ float2 f2u(uint32_t x, uint32_t y) {
   return make_float2(__uint_as_float(x), __uint_as_float(y));

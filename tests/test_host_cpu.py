@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_library_host_only_calls():
     lib = _lib.load()
-    assert lib.tda_version() == 100
+    assert lib.tda_version() == 101
     # workspace: per key tensor a key table of 2 x 128 (padded rows) x 17/16
     # floats = 1088 B, rounded up to 256 B
     assert lib.tda_workspace_size(0, _lib.TDA_BF16, 2, 100, 64, 1) == 1280
@@ -72,6 +72,13 @@ def test_library_rejects_bad_arguments_without_launching():
     assert rc == _lib.TDA_ERR_INVALID  # misaligned pointer
     with pytest.raises(ValueError):
         _lib.check(_lib.TDA_ERR_INVALID)
+    # device-lambda entry point: NULL lambda and negative strides are rejected
+    rc = lib.tda_diff_fwd_lambda(16, 16, 16, 16, 16, None, 16, _lib.TDA_BF16, _lib.TDA_BF16, 1, 2, 128, 64, 1.0,
+                                 None, 0, 1, 2.0, 1, None, 0, 16, None)
+    assert rc == _lib.TDA_ERR_INVALID
+    rc = lib.tda_diff_fwd_lambda(16, 16, 16, 16, 16, None, 16, _lib.TDA_BF16, _lib.TDA_BF16, 1, 2, 128, 64, 1.0,
+                                 16, -1, 1, 2.0, 1, None, 0, 16, None)
+    assert rc == _lib.TDA_ERR_INVALID
 
 
 def test_shape_mismatch_asserts_like_reference():
