@@ -62,7 +62,8 @@ WORKLOADS = {
 }
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one main-kernel launch,
-# from one ncu capture of this bench's workload (profiles/dram_traffic__bench_diff8k_rect8k.md)
+# from one ncu capture of this bench's workload (a single-pass capture of those
+# two metrics on the full-size launch)
 MEASURED_TRAFFIC = {"diff8k": 3263129344, "rect8k": 2142068736}
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -304,6 +305,9 @@ def run_reference_triton(args, rank, local, world):
     for _ in range(args.warmup):
         timed()
     torch.cuda.synchronize()
+    clocks = ClockSampler(gpu_smi_id(local))
+    clocks.start()
+    time.sleep(0.4)  # let the sampler start before the timed region
     ms = []
     for _ in range(args.steps):
         a = torch.cuda.Event(enable_timing=True)
@@ -313,6 +317,7 @@ def run_reference_triton(args, rank, local, world):
         b.record()
         torch.cuda.synchronize()
         ms.append(a.elapsed_time(b))
+    clk = clocks.stop()
     total = sum(ms)
     flops = bwd_flops_of(op, B * H, S, D) if args.backward else flops_of(op, B * H, S, D)
     val = flops * args.steps / (total * 1e-3) / 1e12
@@ -326,6 +331,8 @@ def run_reference_triton(args, rank, local, world):
                    "how": "reference public API, CUDA events per step on the current stream; FLOPs are the "
                           "same dense causal algorithmic count as the tda arm",
                    "flops_per_step": flops},
+        "ms_per_step_min": min(ms),
+        "clocks": clk,
     }
     print(json.dumps(line), flush=True)
     return 0
