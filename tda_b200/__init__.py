@@ -3,6 +3,7 @@
 Drop-in for the public API of snap-research/TDA's ``triton_threshold_attention``
 module; see ``tda_b200.triton_threshold_attention`` for the same module name.
 """
+from . import torch_ops  # noqa: F401  (registers the tda:: torch operators)
 from .ops import (  # noqa: F401
     DifferentialThresholdRelaFunction,
     ThresholdRelaFunction,

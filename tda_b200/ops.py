@@ -13,13 +13,16 @@ behaviour:
   fused pass over the keys (one launch instead of two forward kernels plus
   the torch normalize / clamp / combine ops).
 * ``ThresholdRelaFunction`` -- reference :327-469, forward and backward
-  (``rect_backward``: the reference's dQ / dK / dV kernels, :118-324, on CUDA
-  cores in fp32, head_dim 16-128).
+  (``rect_backward``: the reference's dQ / dK / dV kernels, :118-324; bf16 at
+  head_dim 64/128 on the tcgen05 tensor cores, fp32 and head_dim 16/32 in
+  exact fp32 on CUDA cores).
 
-Data path: CUDA tensors only.  bf16 with head_dim 64/128 runs the tcgen05
-tensor-core kernel; fp32 runs the exact-fp32 CUDA-core kernel; other dtypes /
-head dims are widened to fp32 on the device.  There is no CPU fallback: CPU
-tensors raise, and a missing CUDA library raises.
+Forward data path: CUDA tensors only.  bf16 with head_dim 64/128 runs the
+tcgen05 tensor-core kernel; fp32 with head_dim 64/128 runs the tcgen05 kind::tf32
+kernel with three TF32 products per fp32 product (fp32 accuracy); fp32 at
+other head dims runs the exact-fp32 CUDA-core kernel; other dtypes / head dims
+are widened to fp32 on the device.  There is no CPU fallback: CPU tensors
+raise, and a missing CUDA library raises.
 """
 from __future__ import annotations
 
@@ -116,6 +119,50 @@ def _strided_eligible(ts) -> bool:
     return not all(t.is_contiguous() for t in ts)
 
 
+def _device_lambda(lam, B: int, H: int, device):
+    """A tensor lambda that varies at most over (batch, head), as an fp32
+    device tensor and its element strides (batch, head), 0 for a broadcast
+    dimension.  None for a host scalar (a float or a one-element CPU tensor,
+    read once like the reference reads its scalars) and for a lambda that
+    varies along the sequence or head_dim axes (or has more than 4 dims)."""
+    if not isinstance(lam, torch.Tensor) or lam.dim() > 4:
+        return None
+    if not lam.is_cuda and lam.numel() == 1:
+        return None
+    l4 = lam[(None,) * (4 - lam.dim())]
+    if l4.shape[2] != 1 or l4.shape[3] != 1 or l4.shape[0] not in (1, B) or l4.shape[1] not in (1, H):
+        return None
+    if l4.device != device or l4.dtype != torch.float32:
+        l4 = l4.to(device=device, dtype=torch.float32)
+    sb = l4.stride(0) if l4.shape[0] != 1 else 0
+    sh = l4.stride(1) if l4.shape[1] != 1 else 0
+    return l4, sb, sh
+
+
+def _diff_lambda_call(ts, strided, kind, out, lam_dev, beta_v, p_v, normalize):
+    """tda_diff_fwd_lambda: the fused differential forward with lambda read on
+    the device per (batch, head)."""
+    import ctypes
+    B, H, S, D = ts[0].shape
+    lib = _lib.load()
+    lt, sb, sh = lam_dev
+    ws_n = lib.tda_workspace_size(1, kind, B * H, S, D, int(normalize))
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=out.device) if ws_n else None
+    strides = None
+    if strided:
+        strides = (ctypes.c_int64 * 15)(*[x for t in ts for x in t.stride()[:3]])
+    out_kind = _lib.TDA_F32 if out.dtype == torch.float32 else _lib.TDA_BF16
+    stream = torch.cuda.current_stream(out.device).cuda_stream
+    with torch.cuda.device(out.device):
+        rc = lib.tda_diff_fwd_lambda(*[t.data_ptr() for t in ts],
+                                     ctypes.cast(strides, ctypes.c_void_p) if strides is not None else None,
+                                     out.data_ptr(), kind, out_kind, B, H, S, D, beta_v, lt.data_ptr(), sb, sh, p_v,
+                                     int(normalize), ws.data_ptr() if ws is not None else None, ws_n,
+                                     _status_word(out.device).data_ptr(), stream)
+    _lib.check(rc)
+    return out
+
+
 def _strided_call(entry, ts, out_dtype, extra, normalize, differential):
     import ctypes
     B, H, S, D = ts[0].shape
@@ -172,21 +219,37 @@ def rect_forward(q, k, v, beta, relu_power=2.0, normalize: bool = False, out_dty
 
 def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normalize: bool = True,
                  out_dtype=None) -> torch.Tensor:
-    """Threshold differential attention forward (no autograd), fused."""
+    """Threshold differential attention forward (no autograd), fused.
+
+    lambda_param: a float, or a tensor broadcastable against the output.  A
+    host scalar (float, one-element CPU tensor) is read once; a CUDA tensor
+    that varies at most over (batch, head) -- a scalar, per head or per
+    (batch, head) -- is read by the kernel itself (no host synchronisation,
+    one fused pass); a lambda that also varies along the sequence or head_dim
+    axes runs the two branches separately and combines them as the reference
+    does (:516-517)."""
     assert q1.shape == q2.shape == k1.shape == k2.shape == v.shape
     beta_v = _scalar(beta)
     p_v = _scalar(relu_power)
-    if isinstance(lambda_param, torch.Tensor) and lambda_param.numel() != 1:
-        # A broadcastable (e.g. per-head) lambda: the reference's combine
-        # out1 - clamp(lambda) * out2 (:516-517) applied to two fused passes.
-        o1 = rect_forward(q1, k1, v, beta_v, p_v, normalize, out_dtype=torch.float32)
-        o2 = rect_forward(q2, k2, v, beta_v, p_v, normalize, out_dtype=torch.float32)
-        lam = torch.clamp(lambda_param.to(device=o1.device, dtype=torch.float32), min=0.0, max=1.0)
-        return _finish(o1 - lam * o2, q1.dtype, out_dtype)
-    lam_v = _scalar(lambda_param)
+    lam_dev = None
+    if isinstance(lambda_param, torch.Tensor) and q1.dim() == 4 and q1.is_cuda:
+        lam_dev = _device_lambda(lambda_param, q1.shape[0], q1.shape[1], q1.device)
+        if lam_dev is None and lambda_param.numel() != 1:
+            # lambda varying along the sequence / head_dim axes: the
+            # reference's combine out1 - clamp(lambda) * out2 on two passes
+            o1 = rect_forward(q1, k1, v, beta_v, p_v, normalize, out_dtype=torch.float32)
+            o2 = rect_forward(q2, k2, v, beta_v, p_v, normalize, out_dtype=torch.float32)
+            lam = torch.clamp(lambda_param.to(device=o1.device, dtype=torch.float32), min=0.0, max=1.0)
+            return _finish(o1 - lam * o2, q1.dtype, out_dtype)
     if _strided_eligible([q1, q2, k1, k2, v]):
-        out = _strided_call("tda_diff_fwd_strided", [q1, q2, k1, k2, v], out_dtype, (beta_v, lam_v, p_v), normalize,
-                            True)
+        if lam_dev is not None:
+            B, H, S, D = q1.shape
+            out = torch.empty((B, H, S, D), dtype=torch.float32 if out_dtype == torch.float32 else torch.bfloat16,
+                              device=q1.device)
+            out = _diff_lambda_call([q1, q2, k1, k2, v], True, _lib.TDA_BF16, out, lam_dev, beta_v, p_v, normalize)
+            return _finish(out, q1.dtype, out_dtype)
+        out = _strided_call("tda_diff_fwd_strided", [q1, q2, k1, k2, v], out_dtype,
+                            (beta_v, _scalar(lambda_param), p_v), normalize, True)
         return _finish(out, q1.dtype, out_dtype)
     kind, (a, b, c, d, e), orig = _plan([q1, q2, k1, k2, v], "differential_threshold_rela_triton")
     B, H, S, D = a.shape
@@ -194,6 +257,10 @@ def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normaliz
     out = torch.empty((B, H, S, D), dtype=raw_dt, device=a.device)
     if out.numel() == 0:
         return _finish(out, orig, out_dtype)
+    if lam_dev is not None:
+        out = _diff_lambda_call([a, b, c, d, e], False, kind, out, lam_dev, beta_v, p_v, normalize)
+        return _finish(out, orig, out_dtype)
+    lam_v = _scalar(lambda_param)
     lib = _lib.load()
     ws_n = lib.tda_workspace_size(1, kind, B * H, S, D, int(normalize))
     ws = torch.empty(ws_n, dtype=torch.uint8, device=a.device) if ws_n else None
@@ -250,6 +317,45 @@ def rect_backward(q, k, v, dout, beta, relu_power=2.0, normalize: bool = False, 
     return dq, dk, dv
 
 
+def rect_grads(q, k, v, dout, beta, relu_power, normalize):
+    """(dq, dk, dv) of ``rect_forward(q, k, v, beta, relu_power, normalize)``
+    for the upstream gradient ``dout``, in the inputs' dtypes (reference
+    ThresholdRelaFunction.backward :405-469)."""
+    dq, dk, dv = rect_backward(q, k, v, dout, beta, relu_power, normalize)
+    return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
+
+
+def diff_grads(q1, q2, k1, k2, v, dout, beta, lambda_param, relu_power, normalize, need_dlam: bool):
+    """(dq1, dq2, dk1, dk2, dv, dlambda) of the differential form for the
+    upstream gradient ``dout``: each branch through the branch backward (branch
+    2 with -clamp(lambda) * dout, dv summed), and d lambda = -sum(out2 * dout)
+    where torch.clamp passes the gradient (0 <= lambda <= 1), as torch
+    autograd gives it around the reference (:512-517).  ``lambda_param`` is a
+    float or a tensor; dlambda (lambda's shape and dtype) only when
+    ``need_dlam`` and lambda is a tensor, else None."""
+    lam_t = lambda_param if isinstance(lambda_param, torch.Tensor) else None
+    dq1, dk1, dv = rect_backward(q1, k1, v, dout, beta, relu_power, normalize)
+    if lam_t is None or (lam_t.numel() == 1 and not lam_t.is_cuda):
+        lam = float(lambda_param) if lam_t is None else _scalar(lam_t)
+        lamc = min(max(lam, 0.0), 1.0)
+        dq2, dk2, dv = rect_backward(q2, k2, v, dout, beta, relu_power, normalize, dout_scale=-lamc, dv=dv)
+    else:
+        # tensor lambda (on the device, or broadcast): the second branch
+        # sees -clamp(lambda) * dout, formed without reading lambda on the host
+        lamc = torch.clamp(lam_t.to(device=dout.device, dtype=torch.float32), min=0.0, max=1.0)
+        d2 = (-lamc * dout.float()).contiguous()
+        dq2, dk2, dv = rect_backward(q2, k2, v, d2, beta, relu_power, normalize, dv=dv)
+    dlam = None
+    if lam_t is not None and need_dlam:
+        o2 = rect_forward(q2, k2, v, beta, relu_power, normalize, out_dtype=torch.float32)
+        g = -(o2 * dout.float())
+        lam32 = lam_t.to(device=dout.device, dtype=torch.float32)
+        inside = ((lam32 >= 0.0) & (lam32 <= 1.0)).to(torch.float32)
+        dlam = (g.sum() * inside if lam_t.numel() == 1 else g.sum_to_size(lam_t.shape) * inside)
+        dlam = dlam.reshape(lam_t.shape).to(device=lam_t.device, dtype=lam_t.dtype)
+    return (dq1.to(q1.dtype), dq2.to(q2.dtype), dk1.to(k1.dtype), dk2.to(k2.dtype), dv.to(v.dtype), dlam)
+
+
 class ThresholdRelaFunction(torch.autograd.Function):
     """Threshold Rectified Attention (reference :327-469).
 
@@ -269,16 +375,13 @@ class ThresholdRelaFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v = ctx.saved_tensors
-        dq, dk, dv = rect_backward(q, k, v, dout, ctx.beta, ctx.relu_power, ctx.normalize)
-        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None
+        dq, dk, dv = rect_grads(q, k, v, dout, ctx.beta, ctx.relu_power, ctx.normalize)
+        return dq, dk, dv, None, None, None
 
 
 class DifferentialThresholdRelaFunction(torch.autograd.Function):
-    """Fused threshold differential attention.  Backward: each branch through
-    the branch backward (branch 2 with -clamp(lambda) * dout, dv summed), and
-    d lambda = -sum(out2 * dout) where torch.clamp passes the gradient
-    (0 <= lambda <= 1), as torch autograd gives it around the reference
-    (:512-517)."""
+    """Fused threshold differential attention as an autograd Function
+    (gradients: ``diff_grads``)."""
 
     @staticmethod
     def forward(ctx, q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize):
@@ -294,27 +397,10 @@ class DifferentialThresholdRelaFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         q1, q2, k1, k2, v, lam_t = ctx.saved_tensors
-        beta, p, norm = ctx.beta, ctx.relu_power, ctx.normalize
-        dq1, dk1, dv = rect_backward(q1, k1, v, dout, beta, p, norm)
-        if lam_t is None or lam_t.numel() == 1:
-            lam = ctx.lam_float if lam_t is None else _scalar(lam_t)
-            lamc = min(max(lam, 0.0), 1.0)
-            dq2, dk2, dv = rect_backward(q2, k2, v, dout, beta, p, norm, dout_scale=-lamc, dv=dv)
-        else:
-            # broadcastable lambda: the second branch sees -clamp(lambda) * dout
-            lamc = torch.clamp(lam_t.to(device=dout.device, dtype=torch.float32), min=0.0, max=1.0)
-            d2 = (-lamc * dout.float()).contiguous()
-            dq2, dk2, dv = rect_backward(q2, k2, v, d2, beta, p, norm, dv=dv)
-        dlam = None
-        if lam_t is not None and ctx.needs_input_grad[6]:
-            o2 = rect_forward(q2, k2, v, beta, p, norm, out_dtype=torch.float32)
-            g = -(o2 * dout.float())
-            lam32 = lam_t.to(device=dout.device, dtype=torch.float32)
-            inside = ((lam32 >= 0.0) & (lam32 <= 1.0)).to(torch.float32)
-            dlam = (g.sum() * inside if lam_t.numel() == 1 else g.sum_to_size(lam_t.shape) * inside)
-            dlam = dlam.reshape(lam_t.shape).to(device=lam_t.device, dtype=lam_t.dtype)
-        return (dq1.to(q1.dtype), dq2.to(q2.dtype), dk1.to(k1.dtype), dk2.to(k2.dtype), dv.to(v.dtype), None, dlam,
-                None, None)
+        lam = ctx.lam_float if lam_t is None else lam_t
+        g = diff_grads(q1, q2, k1, k2, v, dout, ctx.beta, lam, ctx.relu_power, ctx.normalize,
+                       ctx.needs_input_grad[6])
+        return g[0], g[1], g[2], g[3], g[4], None, g[5], None, None
 
 
 def threshold_rela_triton(q, k, v, beta, relu_power=2.0, normalize=False):
@@ -323,13 +409,17 @@ def threshold_rela_triton(q, k, v, beta, relu_power=2.0, normalize=False):
     q, k, v: (batch, num_heads, seq_len, head_dim); beta: scalar tensor or
     float; relu_power: scalar (default 2.0); normalize: L2-normalize q and k
     first (default False, the reference's behaviour).  Returns a tensor of
-    q's shape and dtype."""
-    return ThresholdRelaFunction.apply(q, k, v, beta, relu_power, normalize)
+    q's shape and dtype.  Runs as the torch operator ``tda::rect_fwd``
+    (differentiable, traceable by torch.compile)."""
+    return torch.ops.tda.rect_fwd(q, k, v, _scalar(beta), _scalar(relu_power), bool(normalize))
 
 
 def differential_threshold_rela_triton(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normalize=True):
     """Threshold Differential Attention:
     out = TRA(q1, k1, v) - clamp(lambda, 0, 1) * TRA(q2, k2, v), with q/k
-    L2-normalized when ``normalize`` (default True).  Returns q1's shape and
-    dtype."""
-    return DifferentialThresholdRelaFunction.apply(q1, q2, k1, k2, v, beta, lambda_param, relu_power, normalize)
+    L2-normalized when ``normalize`` (default True).  lambda_param: a tensor
+    broadcastable against the output (a float is accepted too).  Returns
+    q1's shape and dtype.  Runs as the torch operator ``tda::diff_fwd``
+    (differentiable, traceable by torch.compile)."""
+    lam = lambda_param if isinstance(lambda_param, torch.Tensor) else torch.tensor(float(lambda_param))
+    return torch.ops.tda.diff_fwd(q1, q2, k1, k2, v, _scalar(beta), lam, _scalar(relu_power), bool(normalize))
