@@ -511,10 +511,13 @@ def run_tda(args, rank, local, world):
     strides = (ctypes.c_int64 * (3 * len(xs)))(*[st for x in xs for st in x.stride()[:3]])
 
     def launch_norms():
+        # the key tables of k (rect) or of k1 and k2 (diff, one launch)
         if separate_norms:
-            ks = (ptr[2], ptr[3]) if op == "diff" else (ptr[1],)
-            for kp, r in zip(ks, rk):
-                _lib.check(lib.tda_key_inv_norms(kp, _lib.TDA_BF16, n_bh, S, D, r.data_ptr(), sp))
+            if op == "diff":
+                _lib.check(lib.tda_key_inv_norms_pair(ptr[2], ptr[3], _lib.TDA_BF16, n_bh, S, D, rk[0].data_ptr(),
+                                                      rk[1].data_ptr(), sp))
+            else:
+                _lib.check(lib.tda_key_inv_norms(ptr[1], _lib.TDA_BF16, n_bh, S, D, rk[0].data_ptr(), sp))
 
     def launch_main():
         if f32:
@@ -541,7 +544,7 @@ def run_tda(args, rank, local, world):
 
     n_br = 2 if op == "diff" else 1
     tf32 = f32 and D in (64, 128)  # fp32 on the tensor cores: one split pre-pass launch and the forward
-    launches_per_step = 2 if tf32 else n_br * int(norm and not f32) + 1
+    launches_per_step = 2 if tf32 else int(norm and not f32) + 1
 
     for _ in range(args.warmup):
         launch_norms()

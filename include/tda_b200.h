@@ -17,9 +17,9 @@
  *   - q, k, v, out are DEVICE pointers to contiguous (batch*heads, seq_len,
  *     head_dim) row-major arrays, i.e. (B, H, S, D) tensors flattened over
  *     (B, H).  All inputs share one shape (the reference asserts this, :348).
- *   - dtype is TDA_F32 or TDA_BF16 for the inputs; out_dtype is the element
- *     type written to out (equal to dtype, or TDA_F32 to receive the fp32
- *     accumulator of a bf16 computation).
+ *   - dtype is TDA_F32, TDA_BF16 or TDA_F16 for the inputs; out_dtype is the
+ *     element type written to out (equal to dtype, or TDA_F32 to receive the
+ *     fp32 accumulator of a bf16 / fp16 computation).
  *   - Causal, with the reference's mask-to-zero semantics (:79-80):
  *     out_i = sum_j relu(s_ij - tau_i)^p v_j, s_ij = q_i.k_j for j <= i and 0
  *     for j > i, tau_i = beta * sqrt(2 * log(i + 1) / head_dim).
@@ -42,7 +42,10 @@
  *     tda_last_error() (thread-local).
  *
  * Supported: dtype TDA_BF16 with head_dim 64 or 128 runs on the tcgen05
- * tensor cores; dtype TDA_F32 with head_dim 64 or 128, given the workspace
+ * tensor cores; dtype TDA_F16 with head_dim 64 or 128 does too (fp16 operands)
+ * when normalize != 0 and relu_power > 0 with P = relu(z)^p bounded by 16384
+ * (always for beta >= 0; for beta < 0, (1 + |beta| sqrt(2 ln S / D))^p),
+ * else it returns TDA_ERR_UNSUPPORTED; dtype TDA_F32 with head_dim 64 or 128, given the workspace
  * that tda_workspace_size reports, runs on the tcgen05 tensor cores too
  * (three TF32 products per fp32 product, fp32 accuracy); dtype TDA_F32 with
  * head_dim in {16, 32, 64, 128, 256} and no workspace runs the exact-fp32
@@ -61,6 +64,7 @@ extern "C" {
 
 #define TDA_F32 0
 #define TDA_BF16 1
+#define TDA_F16 2
 
 #define TDA_OK 0
 #define TDA_ERR_INVALID (-1)     /* bad argument: shape, dtype, NULL or misaligned pointer */
@@ -181,6 +185,13 @@ int tda_diff_fwd_strided(const void* q1, const void* q2, const void* k1, const v
  * This is the key half of F.normalize (triton_threshold_attention.py:507,509). */
 int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float* rk,
                       void* stream);
+
+/* Stage 1 for the two key tensors of the differential form (k1, k2) in one
+ * launch: the key tables of k1 into rk1 and of k2 into rk2, laid out as for
+ * tda_key_inv_norms (k2 = NULL: k1 only).  dtype TDA_BF16 or TDA_F16.  Key
+ * halves of F.normalize(k1), F.normalize(k2) (triton_threshold_attention.py:507,509). */
+int tda_key_inv_norms_pair(const void* k1, const void* k2, int dtype, int64_t batch_heads, int64_t seq_len,
+                           int64_t head_dim, float* rk1, float* rk2, void* stream);
 
 /* Stage 2 of tda_rect_fwd on the tensor-core path (dtype TDA_BF16), given the
  * key inverse norms from tda_key_inv_norms (ignored, may be NULL, when

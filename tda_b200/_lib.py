@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(_HERE, "lib", "libtda_b200.so")
 
 TDA_F32 = 0
 TDA_BF16 = 1
+TDA_F16 = 2
 
 TDA_OK = 0
 TDA_ERR_INVALID = -1
@@ -33,6 +34,7 @@ SIGNATURES = {
     "tda_rect_fwd": (_I, [_P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _F, _F, _I, _P, _SZ, _P, _P]),
     "tda_diff_fwd": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _F, _F, _F, _I, _P, _SZ, _P, _P]),
     "tda_key_inv_norms": (_I, [_P, _I, _I64, _I64, _I64, _P, _P]),
+    "tda_key_inv_norms_pair": (_I, [_P, _P, _I, _I64, _I64, _I64, _P, _P, _P]),
     "tda_rect_fwd_tc": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _F, _F, _I, _P, _P, _P]),
     "tda_diff_fwd_tc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _F, _F, _F, _I, _P, _P, _P, _P]),
     "tda_debug_set": (_I, [_I, ctypes.c_uint64]),

@@ -70,7 +70,7 @@ int make_map(CUtensorMap* m, const void* base, int64_t BH, int64_t S, int64_t D)
 // gradients) as 3-D {D, S, BH}; box {128 bytes of elements, 128 rows, 1},
 // 128-B swizzle (the layout the epilogues stage each 128-row tile in before
 // its TMA store).
-int make_out_map(CUtensorMap* m, void* out, bool f32, int64_t BH, int64_t S, int64_t D) {
+int make_out_map(CUtensorMap* m, void* out, bool f32, int64_t BH, int64_t S, int64_t D, bool f16 = false) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const int64_t es = f32 ? 4 : 2;
@@ -78,7 +78,10 @@ int make_out_map(CUtensorMap* m, void* out, bool f32, int64_t BH, int64_t S, int
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * es), static_cast<cuuint64_t>(S * D * es)};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(tda::kTile), 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dims, strides,
+  CUresult r = enc(m,
+                   f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                       : (f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16),
+                   3, out, dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
@@ -94,8 +97,10 @@ struct View {
 
 View contiguous_view(const void* p, int64_t BH, int64_t S, int64_t D) { return View{p, BH * S * D, S * D, D}; }
 
-// View viewed as 4-D {D, S, heads, batches}; box {64, 128, 1, 1}; 128-B swizzle.
-int make_map4(CUtensorMap* m, const View& x, int64_t batches, int64_t heads, int64_t S, int64_t D) {
+// View viewed as 4-D {D, S, heads, batches}; box {64, 128, 1, 1}; 128-B swizzle;
+// 2-byte elements, bf16 or fp16.
+int make_map4(CUtensorMap* m, const View& x, int64_t batches, int64_t heads, int64_t S, int64_t D,
+              bool f16 = false) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(heads),
@@ -104,7 +109,8 @@ int make_map4(CUtensorMap* m, const View& x, int64_t batches, int64_t heads, int
                            static_cast<cuuint64_t>(x.sb * 2)};
   cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tda::kTile), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(x.p), dims, strides, box, estr,
+  CUresult r = enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                   const_cast<void*>(x.p), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
@@ -138,7 +144,25 @@ int check_common(int64_t BH, int64_t S, int64_t D, int* status) {
   return TDA_OK;
 }
 
-bool tc_supported(int dtype, int64_t D) { return dtype == TDA_BF16 && (D == 64 || D == 128); }
+bool tc_supported(int dtype, int64_t D) { return (dtype == TDA_BF16 || dtype == TDA_F16) && (D == 64 || D == 128); }
+
+// fp16 operands: P = relu(z)^p is split into fp16 hi + lo after a power-of-two
+// scale, so it needs a bound.  With normalize, z = cos - tau <= 1 + max(0, -tau_max),
+// tau_max = |beta| sqrt(2 ln S / D), and |P| <= z_max^p (the differential form's
+// P1 - lambda P2 too).  Returns the scale 2^e (e <= 14) that keeps |P| * scale
+// <= 16384, or 0 when fp16 cannot carry this configuration (no normalize,
+// p <= 0, or a bound above 16384).
+float fp16_p_scale(int normalize, float beta, float p, int64_t S, int64_t D) {
+  if (!normalize || !(p > 0.0f)) return 0.0f;
+  const double tau_max = beta < 0.0f ? -static_cast<double>(beta) * std::sqrt(2.0 * std::log(static_cast<double>(S)) /
+                                                                            static_cast<double>(D))
+                                     : 0.0;
+  const double pmax = std::pow(1.0 + tau_max, static_cast<double>(p));
+  if (!(pmax <= 16384.0)) return 0.0f;
+  int e = static_cast<int>(std::floor(std::log2(16384.0 / pmax)));
+  if (e > 14) e = 14;
+  return std::ldexp(1.0f, e);
+}
 
 // No device lambda: every (batch, head) uses the host scalar.
 constexpr tda::LamSpec kNoLam{nullptr, 0, 0, 1};
@@ -146,11 +170,19 @@ constexpr tda::LamSpec kNoLam{nullptr, 0, 0, 1};
 int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const View& v, void* out, int out_dtype,
            int64_t BH, int64_t heads, int64_t S, int64_t D, float beta, float lam, float p, int normalize,
            const float* rk1, const float* rk2, int* status, void* stream, bool differential,
-           const tda::LamSpec& lam_dev = kNoLam) {
+           const tda::LamSpec& lam_dev = kNoLam, int in_dtype = TDA_BF16) {
   if (int e = check_common(BH, S, D, status)) return e;
   if (heads < 1 || BH % heads != 0) return fail(TDA_ERR_INVALID, "heads must divide batch * heads");
   if (!(D == 64 || D == 128)) return fail(TDA_ERR_UNSUPPORTED, "tensor-core path needs head_dim 64 or 128");
-  if (out_dtype != TDA_BF16 && out_dtype != TDA_F32) return fail(TDA_ERR_INVALID, "out_dtype must be TDA_BF16 or TDA_F32");
+  const bool f16 = in_dtype == TDA_F16;
+  if (out_dtype != in_dtype && out_dtype != TDA_F32)
+    return fail(TDA_ERR_INVALID, "out_dtype must be the input dtype or TDA_F32");
+  float p_scale = 1.0f;
+  if (f16 && (p_scale = fp16_p_scale(normalize, beta, p, S, D)) == 0.0f)
+    return fail(TDA_ERR_UNSUPPORTED,
+                "fp16 inputs run on the tensor cores only with normalize and a bounded ReLU power "
+                "(normalize = %d, beta = %g, relu_power = %g); widen them to fp32",
+                normalize, static_cast<double>(beta), static_cast<double>(p));
   const View* ins[5] = {&q1, &k1, &v, differential ? &q2 : &q1, differential ? &k2 : &k1};
   for (const View* x : ins) {
     if (!x->p || !aligned16(x->p)) return fail(TDA_ERR_INVALID, "inputs must be non-NULL and 16-byte aligned");
@@ -166,14 +198,14 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
   std::memset(&prm, 0, sizeof(prm));
   int e;
   const int64_t batches = BH / heads;
-  if ((e = make_map4(&prm.tm_q1, q1, batches, heads, S, D))) return e;
-  if ((e = make_map4(&prm.tm_k1, k1, batches, heads, S, D))) return e;
-  if ((e = make_map4(&prm.tm_v, v, batches, heads, S, D))) return e;
+  if ((e = make_map4(&prm.tm_q1, q1, batches, heads, S, D, f16))) return e;
+  if ((e = make_map4(&prm.tm_k1, k1, batches, heads, S, D, f16))) return e;
+  if ((e = make_map4(&prm.tm_v, v, batches, heads, S, D, f16))) return e;
   if (differential) {
-    if ((e = make_map4(&prm.tm_q2, q2, batches, heads, S, D))) return e;
-    if ((e = make_map4(&prm.tm_k2, k2, batches, heads, S, D))) return e;
+    if ((e = make_map4(&prm.tm_q2, q2, batches, heads, S, D, f16))) return e;
+    if ((e = make_map4(&prm.tm_k2, k2, batches, heads, S, D, f16))) return e;
   }
-  if ((e = make_out_map(&prm.tm_out, out, out_dtype == TDA_F32, BH, S, D))) return e;
+  if ((e = make_out_map(&prm.tm_out, out, out_dtype == TDA_F32, BH, S, D, f16))) return e;
   prm.rk1 = rk1;
   prm.rk2 = rk2;
   prm.out = out;
@@ -191,10 +223,12 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
   prm.lam_root = p == 2.0f ? std::sqrt(lam) : (p == 3.0f ? std::cbrt(lam) : lam);
   prm.lam_dev = lam_dev;
   prm.tau_scale = 2.0f / static_cast<float>(D);
+  prm.p_scale = p_scale;
+  prm.o_unscale = 1.0f / p_scale;
   prm.timeout_ns = g_timeout_ns.load();
   prm.inject = g_inject.load();
   cudaError_t ce = tda::launch_tc_fwd(prm, static_cast<int>(D), differential, normalize != 0, tda::pow_mode_of(p),
-                                      static_cast<cudaStream_t>(stream));
+                                      f16, static_cast<cudaStream_t>(stream));
   if (ce == cudaErrorLaunchOutOfResources && !g_last_error.empty() &&
       g_last_error.rfind("tensor-core kernel does not fit", 0) == 0)
     return TDA_ERR_CUDA;
@@ -320,16 +354,24 @@ size_t tda_workspace_size(int differential, int dtype, int64_t batch_heads, int6
   return differential ? 2 * one : one;
 }
 
-int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float* rk,
-                      void* stream) {
+int tda_key_inv_norms_pair(const void* k1, const void* k2, int dtype, int64_t batch_heads, int64_t seq_len,
+                           int64_t head_dim, float* rk1, float* rk2, void* stream) {
   if (batch_heads < 1 || seq_len < 1) return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1");
-  if (!tc_supported(dtype, head_dim)) return fail(TDA_ERR_UNSUPPORTED, "key norms need bf16 with head_dim 64 or 128");
-  if (!k || !rk || !aligned16(k) || !aligned16(rk)) return fail(TDA_ERR_INVALID, "k / rk must be 16-byte aligned");
-  cudaError_t ce = tda::launch_key_norms(k, 1, rk, static_cast<int>(batch_heads), static_cast<int>(seq_len),
-                                         static_cast<int>(tda::padded_seq(seq_len)), static_cast<int>(head_dim),
-                                         static_cast<cudaStream_t>(stream));
+  if (batch_heads * tda::padded_seq(seq_len) > 0x7fffffffll) return fail(TDA_ERR_INVALID, "key table too large");
+  if (!tc_supported(dtype, head_dim))
+    return fail(TDA_ERR_UNSUPPORTED, "key norms need bf16 or fp16 with head_dim 64 or 128");
+  if (!k1 || !rk1 || !aligned16(k1) || !aligned16(rk1) || (k2 && (!rk2 || !aligned16(k2) || !aligned16(rk2))))
+    return fail(TDA_ERR_INVALID, "k / rk must be 16-byte aligned");
+  cudaError_t ce = tda::launch_key_norms_pair(k1, k2, dtype, rk1, k2 ? rk2 : nullptr, static_cast<int>(batch_heads),
+                                              static_cast<int>(seq_len), static_cast<int>(tda::padded_seq(seq_len)),
+                                              static_cast<int>(head_dim), static_cast<cudaStream_t>(stream));
   if (ce != cudaSuccess) return cuda_fail(ce, "key norm launch");
   return TDA_OK;
+}
+
+int tda_key_inv_norms(const void* k, int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float* rk,
+                      void* stream) {
+  return tda_key_inv_norms_pair(k, nullptr, dtype, batch_heads, seq_len, head_dim, rk, nullptr, stream);
 }
 
 int tda_rect_fwd_tc(const void* q, const void* k, const void* v, void* out, int out_dtype, int64_t batch_heads,
@@ -350,6 +392,31 @@ int tda_diff_fwd_tc(const void* q1, const void* q2, const void* k1, const void* 
 }
 
 namespace {
+// Contiguous bf16 / fp16 differential form on the tensor cores: the key tables
+// of k1 and k2 in one launch, then the fused kernel.
+int diff_tc_path(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out, int dtype,
+                 int out_dtype, int64_t BH, int64_t S, int64_t D, float beta, float lam, float p, int normalize,
+                 void* workspace, size_t workspace_bytes, int* status, void* stream, const tda::LamSpec& lam_dev) {
+  if (dtype != TDA_BF16 && dtype != TDA_F16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32, TDA_BF16 or TDA_F16");
+  if (!tc_supported(dtype, D))
+    return fail(TDA_ERR_UNSUPPORTED, "bf16 / fp16 path supports head_dim 64 or 128 (got %lld)", static_cast<long long>(D));
+  if (dtype == TDA_F16 && fp16_p_scale(normalize, beta, p, S, D) == 0.0f)
+    return fail(TDA_ERR_UNSUPPORTED, "fp16 inputs run on the tensor cores only with normalize and a bounded ReLU "
+                                     "power; widen them to fp32");
+  float* rk1 = nullptr;
+  float* rk2 = nullptr;
+  if (normalize) {
+    const size_t need = tda_workspace_size(1, dtype, BH, S, D, normalize);
+    if (!workspace || workspace_bytes < need) return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
+    rk1 = static_cast<float*>(workspace);
+    rk2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2);
+    if (int e = tda_key_inv_norms_pair(k1, k2, dtype, BH, S, D, rk1, rk2, stream)) return e;
+  }
+  auto cv = [&](const void* x) { return contiguous_view(x, BH, S, D); };
+  return run_tc(cv(q1), cv(q2), cv(k1), cv(k2), cv(v), out, out_dtype, BH, BH, S, D, beta, lam, p, normalize, rk1,
+                rk2, status, stream, true, lam_dev, dtype);
+}
+
 // Strided entry points: key tables of the strided keys, then the fused kernel.
 int run_strided(const View* views, int n, void* out, int out_dtype, int64_t batch, int64_t heads, int64_t S,
                 int64_t D, float beta, float lam, float p, int normalize, void* workspace, size_t workspace_bytes,
@@ -380,12 +447,12 @@ int run_strided(const View* views, int n, void* out, int out_dtype, int64_t batc
     rk1 = static_cast<float*>(workspace);
     rk2 = diff ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2) : nullptr;
     const int S_pad = static_cast<int>(tda::padded_seq(S));
-    cudaError_t ce = tda::launch_key_norms_strided(k1.p, rk1, static_cast<int>(BH), static_cast<int>(heads),
-                                                   static_cast<int>(S), S_pad, static_cast<int>(D), k1.sb, k1.sh,
-                                                   k1.ss, st);
-    if (ce == cudaSuccess && diff)
-      ce = tda::launch_key_norms_strided(k2.p, rk2, static_cast<int>(BH), static_cast<int>(heads),
-                                         static_cast<int>(S), S_pad, static_cast<int>(D), k2.sb, k2.sh, k2.ss, st);
+    const void* kx[2] = {k1.p, k2.p};
+    float* const kt[2] = {rk1, rk2};
+    const int64_t sb[2] = {k1.sb, k2.sb}, sh[2] = {k1.sh, k2.sh}, ss[2] = {k1.ss, k2.ss};
+    cudaError_t ce = tda::launch_key_norms_strided(diff ? 2 : 1, kx, kt, TDA_BF16, static_cast<int>(BH),
+                                                   static_cast<int>(heads), static_cast<int>(S), S_pad,
+                                                   static_cast<int>(D), sb, sh, ss, st);
     if (ce != cudaSuccess) return cuda_fail(ce, "key table launch");
   }
   return run_tc(q1, q2, k1, k2, v, out, out_dtype, BH, heads, S, D, beta, lam, p, normalize, rk1, rk2, status, stream,
@@ -431,10 +498,13 @@ int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dty
     return run_simt(q, nullptr, k, nullptr, v, out, batch_heads, seq_len, head_dim, beta, 0.0f, relu_power,
                     normalize, status, stream, false);
   }
-  if (dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
+  if (dtype != TDA_BF16 && dtype != TDA_F16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32, TDA_BF16 or TDA_F16");
   if (!tc_supported(dtype, head_dim))
-    return fail(TDA_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
+    return fail(TDA_ERR_UNSUPPORTED, "bf16 / fp16 path supports head_dim 64 or 128 (got %lld)",
                 static_cast<long long>(head_dim));
+  if (dtype == TDA_F16 && fp16_p_scale(normalize, beta, relu_power, seq_len, head_dim) == 0.0f)
+    return fail(TDA_ERR_UNSUPPORTED, "fp16 inputs run on the tensor cores only with normalize and a bounded ReLU "
+                                     "power; widen them to fp32");
   float* rk = nullptr;
   if (normalize) {
     const size_t need = tda_workspace_size(0, dtype, batch_heads, seq_len, head_dim, normalize);
@@ -443,8 +513,9 @@ int tda_rect_fwd(const void* q, const void* k, const void* v, void* out, int dty
     rk = static_cast<float*>(workspace);
     if (int e = tda_key_inv_norms(k, dtype, batch_heads, seq_len, head_dim, rk, stream)) return e;
   }
-  return tda_rect_fwd_tc(q, k, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, relu_power, normalize, rk,
-                         status, stream);
+  auto cv = [&](const void* x) { return contiguous_view(x, batch_heads, seq_len, head_dim); };
+  return run_tc(cv(q), cv(nullptr), cv(k), cv(nullptr), cv(v), out, out_dtype, batch_heads, batch_heads, seq_len,
+                head_dim, beta, 0.0f, relu_power, normalize, rk, nullptr, status, stream, false, kNoLam, dtype);
 }
 
 int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2, const void* v, void* out,
@@ -460,23 +531,8 @@ int tda_diff_fwd(const void* q1, const void* q2, const void* k1, const void* k2,
     return run_simt(q1, q2, k1, k2, v, out, batch_heads, seq_len, head_dim, beta, clamp01(lambda_param),
                     relu_power, normalize, status, stream, true);
   }
-  if (dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
-  if (!tc_supported(dtype, head_dim))
-    return fail(TDA_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
-                static_cast<long long>(head_dim));
-  float* rk1 = nullptr;
-  float* rk2 = nullptr;
-  if (normalize) {
-    const size_t need = tda_workspace_size(1, dtype, batch_heads, seq_len, head_dim, normalize);
-    if (!workspace || workspace_bytes < need)
-      return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
-    rk1 = static_cast<float*>(workspace);
-    rk2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2);
-    if (int e = tda_key_inv_norms(k1, dtype, batch_heads, seq_len, head_dim, rk1, stream)) return e;
-    if (int e = tda_key_inv_norms(k2, dtype, batch_heads, seq_len, head_dim, rk2, stream)) return e;
-  }
-  return tda_diff_fwd_tc(q1, q2, k1, k2, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, lambda_param,
-                         relu_power, normalize, rk1, rk2, status, stream);
+  return diff_tc_path(q1, q2, k1, k2, v, out, dtype, out_dtype, batch_heads, seq_len, head_dim, beta,
+                      clamp01(lambda_param), relu_power, normalize, workspace, workspace_bytes, status, stream, kNoLam);
 }
 
 size_t tda_bwd_workspace_size(int dtype, int64_t batch_heads, int64_t seq_len, int64_t head_dim, int normalize) {
@@ -600,23 +656,8 @@ int tda_diff_fwd_lambda(const void* q1, const void* q2, const void* k1, const vo
     return run_simt(q1, q2, k1, k2, v, out, BH, seq_len, head_dim, beta, 0.0f, relu_power, normalize, status, stream,
                     true, lam);
   }
-  if (dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
-  if (!tc_supported(dtype, head_dim))
-    return fail(TDA_ERR_UNSUPPORTED, "bf16 path supports head_dim 64 or 128 (got %lld)",
-                static_cast<long long>(head_dim));
-  float* rk1 = nullptr;
-  float* rk2 = nullptr;
-  if (normalize) {
-    const size_t need = tda_workspace_size(1, dtype, BH, seq_len, head_dim, normalize);
-    if (!workspace || workspace_bytes < need) return fail(TDA_ERR_WORKSPACE, "workspace of %zu bytes required", need);
-    rk1 = static_cast<float*>(workspace);
-    rk2 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + need / 2);
-    if (int e = tda_key_inv_norms(k1, dtype, BH, seq_len, head_dim, rk1, stream)) return e;
-    if (int e = tda_key_inv_norms(k2, dtype, BH, seq_len, head_dim, rk2, stream)) return e;
-  }
-  auto cv = [&](const void* x) { return contiguous_view(x, BH, seq_len, head_dim); };
-  return run_tc(cv(q1), cv(q2), cv(k1), cv(k2), cv(v), out, out_dtype, BH, BH, seq_len, head_dim, beta, 0.0f,
-                relu_power, normalize, rk1, rk2, status, stream, true, lam);
+  return diff_tc_path(q1, q2, k1, k2, v, out, dtype, out_dtype, BH, seq_len, head_dim, beta, 0.0f, relu_power,
+                      normalize, workspace, workspace_bytes, status, stream, lam);
 }
 
 }  // extern "C"

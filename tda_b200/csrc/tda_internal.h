@@ -74,13 +74,17 @@ struct TcFwdParams {
   float lam_root;     // lambda^(1/p) for p in {1, 2, 3} (folded into the second branch)
   LamSpec lam_dev;    // per-(batch, head) lambda on the device (ptr null: lam / lam_root)
   float tau_scale;    // 2 / D
+  float p_scale;      // fp16 inputs: P is multiplied by this power of two before its fp16 split
+  float o_unscale;    // fp16 inputs: 1 / p_scale, applied to O in the epilogue
   unsigned long long timeout_ns;
   int inject;         // test hook: bit 0 = producer never loads Q (forces a timeout)
   unsigned* item_ctr;  // persistent kernel: zeroed work-item counter (null: one CTA per query tile)
 };
 
+// fp16 = true: q, k, v (and the output, unless fp32) are fp16 -- kind::f16 with
+// fp16 operands, P split into fp16 hi + lo; only with normalize (P bounded).
 cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,
-                          cudaStream_t stream);
+                          bool fp16, cudaStream_t stream);
 
 
 // CUDA-core fp32 forward (exact fp32 FFMA), any power-of-two D in [16, 256].
@@ -246,12 +250,17 @@ cudaError_t launch_tc_bwd(const TcBwdParams& p, int head_dim, bool normalize, in
 // Key table of x: rk[bh][j] = 1 / max(||x[bh][j]||_2, 1e-12) for j < S, 0 for
 // S <= j < S_pad, followed by rkmax[bh][g] = max of rk over keys [16 g, 16 g + 16).
 inline size_t key_table_floats(int64_t BH, int64_t S) { return static_cast<size_t>(BH) * padded_seq(S) / 16 * 17; }
-cudaError_t launch_key_norms(const void* x, int x_is_bf16, float* rk, int BH, int S, int S_pad, int D,
+// dtype: 1 = bf16, 2 = fp16 (the TDA_BF16 / TDA_F16 codes).
+cudaError_t launch_key_norms(const void* x, int dtype, float* rk, int BH, int S, int S_pad, int D,
                              cudaStream_t stream);
-// Same for a strided (batch, head, seq, dim) view (strides in elements, last
-// dimension contiguous); bh = b * heads + h.
-cudaError_t launch_key_norms_strided(const void* x, float* rk, int BH, int heads, int S, int S_pad, int D,
-                                     int64_t stride_b, int64_t stride_h, int64_t stride_s, cudaStream_t stream);
+// Both key tensors of the differential form in one launch (x2 = nullptr: x1 only).
+cudaError_t launch_key_norms_pair(const void* x1, const void* x2, int dtype, float* rk1, float* rk2, int BH, int S,
+                                  int S_pad, int D, cudaStream_t stream);
+// Same for n (1 or 2) strided (batch, head, seq, dim) views (strides in
+// elements, last dimension contiguous); bh = b * heads + h.
+cudaError_t launch_key_norms_strided(int n, const void* const x[2], float* const rk[2], int dtype, int BH, int heads,
+                                     int S, int S_pad, int D, const int64_t stride_b[2], const int64_t stride_h[2],
+                                     const int64_t stride_s[2], cudaStream_t stream);
 
 // Sets the thread-local message returned by tda_last_error().
 void set_last_error(const char* msg);

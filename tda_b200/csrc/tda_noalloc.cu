@@ -12,8 +12,9 @@
 // The first call on each device looks up the array's device address (the
 // set-up step); make that first call before capturing the stream into a CUDA
 // graph.  The array below is reserved on every GPU that loads the library, for
-// the life of the process (8.5 MiB).  It holds the inverse key norms of k1 and k2,
-// so it limits batch_heads * round_up(seq_len, 128) to kNoAllocMaxRows.
+// the life of the process (8.5 MiB).  It holds the inverse key norms of k1 and k2
+// (it is passed to tda_diff_fwd as its workspace), so it limits
+// batch_heads * round_up(seq_len, 128) to kNoAllocMaxRows.
 //
 // All calls share the one array and it keeps whatever the last call wrote.
 // Nothing in it has to start at zero: each call's norm pass rewrites every
@@ -93,10 +94,8 @@ extern "C" int tda_diff_fwd_noalloc(const void* q1, const void* q2, const void* 
   float* scratch = nullptr;
   int rc = scratch_on_current_device(&scratch);
   if (rc != TDA_OK) return rc;
-  float* rk1 = scratch;
-  float* rk2 = scratch + kTableFloats;
-  if ((rc = tda_key_inv_norms(k1, dtype, batch_heads, seq_len, head_dim, rk1, stream)) != TDA_OK) return rc;
-  if ((rc = tda_key_inv_norms(k2, dtype, batch_heads, seq_len, head_dim, rk2, stream)) != TDA_OK) return rc;
-  return tda_diff_fwd_tc(q1, q2, k1, k2, v, out, out_dtype, batch_heads, seq_len, head_dim, beta, lambda_param,
-                         relu_power, normalize, rk1, rk2, status, stream);
+  // The array serves as tda_diff_fwd's workspace: it holds that call's two
+  // key tables (bf16 or fp16 keys) for any size within the limit above.
+  return tda_diff_fwd(q1, q2, k1, k2, v, out, dtype, out_dtype, batch_heads, seq_len, head_dim, beta, lambda_param,
+                      relu_power, normalize, scratch, sizeof(g_noalloc_scratch), status, stream);
 }

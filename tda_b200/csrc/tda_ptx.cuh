@@ -307,6 +307,30 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
+// Pack two floats to f16x2 (round to nearest even); `lo` goes in bits 0-15.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// The two halves of an f16x2 word as floats (bits 0-15 in .x).
+__device__ __forceinline__ float2 unpack_f16x2(uint32_t w) {
+  float lo, hi;
+  asm("{\n\t.reg .b16 l, h;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "cvt.f32.f16 %0, l;\n\t"
+      "cvt.f32.f16 %1, h;\n\t}\n"
+      : "=f"(lo), "=f"(hi)
+      : "r"(w));
+  return make_float2(lo, hi);
+}
+
+// The two halves of a bf16x2 word as floats (bits 0-15 in .x): exact.
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
 __device__ __forceinline__ float fast_lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -47,9 +47,11 @@ namespace {
 
 using namespace tc;
 
-constexpr int kTransformWG = 2;                    // transform warpgroups
-constexpr int kTransformWarps = 4 * kTransformWG;  // warps 2 .. 9
-// differential form: warp 10 issues the QK2 products (second MMA issuer)
+// Persistent kernel: two transform warpgroups (warps 2 .. 9), each thread two
+// 32-key chunks of every key tile; differential form: warp 10 issues the QK2
+// products (second MMA issuer).
+constexpr int kTransformWG = 2;
+constexpr int kTransformWarps = 4 * kTransformWG;
 constexpr int kQk2Warp = 2 + kTransformWarps;
 template <bool DIFF>
 constexpr int threads_for() { return 32 * (2 + kTransformWarps + (DIFF ? 1 : 0)); }
@@ -70,8 +72,21 @@ constexpr int ST_PROD_SLOT = 0x101, ST_PROD_RK = 0x102;
 constexpr int ST_MMA_Q = 0x201, ST_MMA_SLOT = 0x202, ST_MMA_P = 0x203, ST_MMA_S2 = 0x204;
 constexpr int ST_TR_Q = 0x301, ST_TR_RK = 0x302, ST_TR_S = 0x303, ST_TR_O = 0x304;
 
+// One-CTA-per-tile kernel: two transform warpgroups (warps 2 .. 9), each
+// thread two 32-key chunks of every key tile.  The MMAs come from two
+// single-thread issuers so that one issuer's waits and commits (each some
+// 100-200 cycles of latency on a single thread) overlap the other's MMAs:
+// warp 1 issues every PV (and QK1 for the differential form), warp 10 the QK
+// products (rect) or QK2 (differential).  (Four warpgroups with one chunk per thread --
+// kTWG = 4, which this code also supports -- measured 4-8% slower on B200:
+// the transform's per-warp instruction latency is not what bounds a tile.)
 template <int D, bool DIFF>
 struct Cfg {
+  static constexpr int kTWG = 2;                 // transform warpgroups
+  static constexpr int kTW = 4 * kTWG;           // transform warps 2 .. 1 + kTW
+  static constexpr int kQk2W = 2 + kTW;          // QK issuer (rect) / QK2 issuer (differential)
+  static constexpr int kThreads = 32 * (3 + kTW);
+  static constexpr int kMaxRegs = kTWG == 2 ? 168 : 96;  // per-thread register cap of the launch
   static constexpr int kBoxes = D / 64;
   static constexpr int kBoxBytes = kTile * 128;  // 128 rows x 64 bf16 (128 B)
   static constexpr int kTileBytes = kTile * D * 2;
@@ -79,7 +94,7 @@ struct Cfg {
   static constexpr int kRkPerTile = (DIFF ? 2 : 1) * (kTile + 8);  // rk then per-16-key maxima
   static constexpr int kRkFloats = kRkRing * kRkPerTile;
   static constexpr int kBarBytes = 1024;
-  static constexpr int kQssBytes = kNQ * kTransformWG * kTile * 4;  // partial sums of ||q||^2
+  static constexpr int kQssBytes = kNQ * kTWG * kTile * 4;  // partial sums of ||q||^2
   static constexpr int kFixed = kNQ * kTileBytes + kRkFloats * 4 + kBarBytes + kQssBytes + 1024;
   static constexpr int kSlotsRaw = (kSmemBudget - kFixed) / kTileBytes;
   static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
@@ -97,17 +112,16 @@ struct Cfg {
   static __device__ __forceinline__ uint32_t col_s(int slot) {
     return DIFF ? (slot ? 256u : 0u) : static_cast<uint32_t>(slot * 128);
   }
-  static constexpr uint32_t kIdescQK = idesc_f16(128, 128, true, false);
-  static constexpr uint32_t kIdescPV = idesc_f16(128, D, true, true);
 };
 
 struct Bars {
   uint64_t q_full;
   uint64_t o_full;
-  uint64_t drain;
-  uint64_t drain2;      // differential: the QK2 issuer's own MMAs
-  uint64_t s_full[3];   // per S slot; differential: one arrival per MMA issuer
+  uint64_t drain;       // warp 1's own MMAs (abort)
+  uint64_t drain2;      // the QK (rect) / QK2 (differential) issuer's own MMAs
+  uint64_t s_full[3];   // per S slot; differential: one arrival per QK issuer
   uint64_t p_full[3];
+  uint64_t pv_done[3];  // rect, per S slot: the PV reading P from it has run
   uint64_t s2_free[2];  // differential: every transform warp has read S2 of the tile
   uint64_t rk_full[kRkRing];
   uint64_t rk_empty[kRkRing];
@@ -265,8 +279,11 @@ __device__ __forceinline__ int ring_v(int j, int n_kt) { return j <= n_kt - 2 ? 
 
 // C: shared-memory layout (ring, box and tile sizes, TMEM columns); B: the
 // barrier block (slot_full / slot_empty / tile_mask) of the kernel using it.
-template <int D, bool DIFF, class C = Cfg<D, DIFF>, class B = Bars>
+template <int D, bool DIFF, class C = Cfg<D, DIFF>, class B = Bars, bool F16 = false>
 struct MmaIssuer {
+  // kind::f16 instruction descriptors: bf16 or fp16 operands, f32 accumulation
+  static constexpr uint32_t kIdQK = idesc_f16(128, 128, !F16, false);
+  static constexpr uint32_t kIdPV = idesc_f16(128, D, !F16, true);
   B* bars;
   const WaitCtl& ctl;
   uint32_t tmem;
@@ -286,15 +303,16 @@ struct MmaIssuer {
     return slot;
   }
   // S[dcol] = Q K^T over D in UMMA_K = 16 steps (32 B inside a 128-B swizzled row)
-  __device__ void qk(int idx, uint32_t dcol, uint32_t q_base) {
-    const int slot = acquire(idx);
+  __device__ void qk(int idx, uint32_t dcol, uint32_t q_base) { qk_at(acquire(idx), dcol, q_base); }
+  // the same with K already in ring slot `slot` (acquired)
+  __device__ void qk_at(int slot, uint32_t dcol, uint32_t q_base) {
     if (!ok) return;
     const uint32_t k_base = ring_base + slot * C::kTileBytes;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const uint32_t off = (kk >> 2) * C::kBoxBytes + (kk & 3) * 32;
       mma_ss(tmem + dcol, smem_desc_sw128(q_base + off, 16, 1024), smem_desc_sw128(k_base + off, 16, 1024),
-             C::kIdescQK, kk > 0 ? 1u : 0u);
+             kIdQK, kk > 0 ? 1u : 0u);
     }
     tc_commit(&bars->slot_empty[slot]);
   }
@@ -303,8 +321,9 @@ struct MmaIssuer {
   // 16-key slabs set in `mask` are multiplied (the others hold P = 0); the
   // first PV of the CTA initialises O (accumulate = 0) and therefore always
   // issues at least its first slab.
-  __device__ void pv(int idx, uint32_t pcol, uint32_t mask) {
-    const int slot = acquire(idx);
+  __device__ void pv(int idx, uint32_t pcol, uint32_t mask) { pv_at(acquire(idx), pcol, mask); }
+  // the same with V already in ring slot `slot` (acquired)
+  __device__ void pv_at(int slot, uint32_t pcol, uint32_t mask) {
     if (!ok) return;
     if (!o_started) mask |= 1u;
     if (mask == 0u) {
@@ -317,8 +336,8 @@ struct MmaIssuer {
       if (!(mask & (1u << m))) continue;
       const uint64_t bdesc = smem_desc_sw128(v_base + m * 2048, C::kBoxBytes, 1024);
       const uint32_t a_hi = tmem + pcol + 32 * (m >> 1) + 8 * (m & 1);
-      mma_ts(tmem + C::kColO, a_hi, bdesc, C::kIdescPV, o_started ? 1u : 0u);
-      mma_ts(tmem + C::kColO, a_hi + 16, bdesc, C::kIdescPV, 1u);
+      mma_ts(tmem + C::kColO, a_hi, bdesc, kIdPV, o_started ? 1u : 0u);
+      mma_ts(tmem + C::kColO, a_hi + 16, bdesc, kIdPV, 1u);
       o_started = true;
     }
     tc_commit(&bars->slot_empty[slot]);
@@ -342,46 +361,47 @@ struct MmaIssuer {
   }
 };
 
-// Main issuer (warp 1): QK (rect) or QK1 (differential) and every PV.
-// rect: three S slots; QK_{j+3} reuses the slot of P_j right after PV_j
-// (the tensor pipe runs one thread's MMAs in order).
-// differential: two S1 slots; the QK2 products come from warp 10.
-template <int D, bool DIFF>
+// Ring position of V_j in the rectified form's load order K0, K1, K2, then per
+// key tile j: V_j, K_{j+3} (K_{j+3} only while j + 3 < n_kt).
+__device__ __forceinline__ int ring_v_rect(int j, int n_kt) {
+  const int ahead = n_kt > 3 ? n_kt - 3 : 0;
+  return (n_kt < 3 ? n_kt : 3) + j + (j < ahead ? j : ahead);
+}
+
+// PV issuer (warp 1): every O += P V, with V_j's ring slot acquired before
+// the wait for P_j (V_j is loaded well ahead, and the data does not depend
+// on P, so this takes the acquire off the path from P_j to PV_j).
+//   rect: after PV_j it commits pv_done of P_j's S slot (arrives once PV_j
+//     has run), which hands the slot to the QK issuer (warp 10).
+//   differential: the same thread also issues QK1_{j+2} into P_j's slot right
+//     after PV_j (the tensor pipe runs one thread's MMAs in order, so no wait
+//     for PV_j is needed).  Its K1 tile is acquired only after PV_j: with four
+//     32 KB ring slots for three tiles per key step the K1 load is often
+//     still in flight, and waiting for it first would hold PV_j back.
+template <int D, bool DIFF, bool F16>
 __device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
   using C = Cfg<D, DIFF>;
-  MmaIssuer<D, DIFF> m(smem, bars, ctl, tmem);
+  MmaIssuer<D, DIFF, C, Bars, F16> m(smem, bars, ctl, tmem);
   const uint32_t q1_base = smem_u32(smem);
-  m.wait(&bars->q_full, 0, ST_MMA_Q);
-  if constexpr (!DIFF) {
-    int ridx = 0;  // ring order: K0, K1, K2, then per j: V_j, K_{j+3}
-    for (int t = 0; t < C::kSSlots && t < n_kt; ++t) {
-      m.qk(ridx++, C::col_s(t), q1_base);
+  if constexpr (DIFF) {
+    m.wait(&bars->q_full, 0, ST_MMA_Q);
+    for (int t = 0; t < 2 && t < n_kt; ++t) {
+      m.qk(ring_k1(t), C::col_s(t), q1_base);
       m.commit(&bars->s_full[t]);
     }
-    for (int j = 0; j < n_kt && m.ok; ++j) {
-      const int slot = j % C::kSSlots;
-      m.wait(&bars->p_full[slot], (j / C::kSSlots) & 1, ST_MMA_P);
-      m.pv(ridx++, C::col_s(slot), m.slab_mask(j));
-      if (j + C::kSSlots < n_kt) {
-        m.qk(ridx++, C::col_s(slot), q1_base);
-        m.commit(&bars->s_full[slot]);
-      }
-    }
-  } else {
-    m.qk(ring_k1(0), C::col_s(0), q1_base);
-    m.commit(&bars->s_full[0]);
-    if (n_kt > 1) {
-      m.qk(ring_k1(1), C::col_s(1), q1_base);
-      m.commit(&bars->s_full[1]);
-    }
-    for (int j = 0; j < n_kt && m.ok; ++j) {
-      const int slot = j & 1;
-      m.wait(&bars->p_full[slot], (j >> 1) & 1, ST_MMA_P);
-      m.pv(ring_v(j, n_kt), C::col_s(slot), m.slab_mask(j));
+  }
+  for (int j = 0; j < n_kt && m.ok; ++j) {
+    const int slot = j % C::kSSlots;
+    const int vslot = m.acquire(DIFF ? ring_v(j, n_kt) : ring_v_rect(j, n_kt));
+    m.wait(&bars->p_full[slot], (j / C::kSSlots) & 1, ST_MMA_P);
+    m.pv_at(vslot, C::col_s(slot), m.slab_mask(j));
+    if constexpr (DIFF) {
       if (j + 2 < n_kt) {
         m.qk(ring_k1(j + 2), C::col_s(slot), q1_base);
         m.commit(&bars->s_full[slot]);
       }
+    } else {
+      m.commit(&bars->pv_done[slot]);
     }
   }
   if (m.ok)
@@ -390,15 +410,38 @@ __device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t 
     m.drain(&bars->drain);
 }
 
+// QK issuer of the rectified form (warp 10).  The first three products go
+// into free S slots; QK_{j+3} waits until PV_j, which reads P_j from the same
+// slot, has run (pv_done), its K slot acquired before that wait.
+template <int D, bool F16>
+__device__ void run_mma_qk(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
+  using C = Cfg<D, false>;
+  MmaIssuer<D, false, C, Bars, F16> m(smem, bars, ctl, tmem);
+  const uint32_t q1_base = smem_u32(smem);
+  m.wait(&bars->q_full, 0, ST_MMA_Q);
+  for (int t = 0; t < C::kSSlots && t < n_kt; ++t) {
+    m.qk(t, C::col_s(t), q1_base);
+    m.commit(&bars->s_full[t]);
+  }
+  for (int j = 0; j + C::kSSlots < n_kt && m.ok; ++j) {
+    const int slot = j % C::kSSlots;
+    const int kslot = m.acquire(ring_v_rect(j, n_kt) + 1);
+    m.wait(&bars->pv_done[slot], (j / C::kSSlots) & 1, ST_MMA_P);
+    m.qk_at(kslot, C::col_s(slot), q1_base);
+    m.commit(&bars->s_full[slot]);
+  }
+  if (!m.ok) m.drain(&bars->drain2);
+}
+
 // Second issuer of the differential form (warp 10): S2 = Q2 K2^T into its
 // single TMEM slot.  The slot is free once every transform warp holds S2_j in
 // registers (s2_free), which happens long before P_j is ready; a separate
 // thread issues these products so that the main issuer, blocked while the
 // tensor pipe accepts its PV and QK1 products, does not delay them.
-template <int D>
+template <int D, bool F16>
 __device__ void run_mma_qk2(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
   using C = Cfg<D, true>;
-  MmaIssuer<D, true> m(smem, bars, ctl, tmem);
+  MmaIssuer<D, true, C, Bars, F16> m(smem, bars, ctl, tmem);
   const uint32_t q2_base = smem_u32(smem) + C::kTileBytes;
   m.wait(&bars->q_full, 0, ST_MMA_Q);
   m.qk(ring_k2(0), C::kColS2, q2_base);
@@ -411,17 +454,17 @@ __device__ void run_mma_qk2(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint3
   if (!m.ok) m.drain(&bars->drain2);
 }
 
-// Transform warps: warp w (2 <= w < 2 + kTransformWarps) owns TMEM lane
-// quarter w % 4 (query rows) and, as warpgroup g = (w - 2) / 4, the key
-// chunks [g kChunks, (g+1) kChunks) of every key tile (32 keys each) and the
-// output columns [g D/kTransformWG, (g+1) D/kTransformWG).
-template <int D, bool DIFF, bool NORM, bool POS, int PM>
+// Transform warps: warp w (2 <= w < 2 + C::kTW) owns TMEM lane quarter w % 4
+// (query rows) and, as warpgroup g = (w - 2) / 4, the key chunks
+// [g kChunks, (g+1) kChunks) of every key tile (32 keys each) and the output
+// columns [g D/kTWG, (g+1) D/kTWG).
+template <int D, bool DIFF, bool NORM, bool POS, int PM, bool F16>
 __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem,
                               int bh, int qt, int n_kt, int warp, int lane) {
   using C = Cfg<D, DIFF>;
   constexpr bool kFold = PM != POW_GENERAL;
-  constexpr int kChunks = 4 / kTransformWG;  // 32-key chunks per thread per tile
-  static_assert(kChunks == 2, "transform_tile handles two chunks");
+  constexpr int kChunks = 4 / C::kTWG;  // 32-key chunks per thread per tile
+  constexpr int kQChunks = 8 / C::kTWG;  // 16-B chunks of each 128-B query row this warpgroup sums
   const int wg = (warp - 2) >> 2;
   const int quarter = warp & 3;
   const int row = quarter * 32 + lane;
@@ -447,7 +490,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     // warpgroups (which own the same rows) each sum half of every row's
     // chunks and exchange the partial sums through shared memory.  A rolled
     // loop keeps this once-per-CTA code small in the instruction cache.
-    float* qss = reinterpret_cast<float*>(smem + C::kOffQss);  // [kNQ][kTransformWG][kTile]
+    float* qss = reinterpret_cast<float*>(smem + C::kOffQss);  // [kNQ][kTWG][kTile]
     if (ok) {
 #pragma unroll 1
       for (int t = 0; t < C::kNQ; ++t) {
@@ -456,31 +499,37 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
         for (int bx = 0; bx < C::kBoxes; ++bx) {
           const uint8_t* rb = smem + t * C::kTileBytes + bx * C::kBoxBytes + row * 128;
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
+          for (int k = 0; k < kQChunks; ++k) {
             // logical chunk cc sits at (cc ^ (row & 7)): for one cc the 8 rows of
             // each group of 8 lanes hit 8 different 16-B bank groups
-            const int cc = 4 * wg + k;
+            const int cc = kQChunks * wg + k;
             const uint4 u = *reinterpret_cast<const uint4*>(rb + ((cc ^ (row & 7)) << 4));
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-              const float lo = __uint_as_float(w[h] << 16), hi = __uint_as_float(w[h] & 0xFFFF0000u);
-              ss = fmaf(lo, lo, ss);
-              ss = fmaf(hi, hi, ss);
+              const float2 x = F16 ? unpack_f16x2(w[h]) : unpack_bf16x2(w[h]);
+              ss = fmaf(x.x, x.x, ss);
+              ss = fmaf(x.y, x.y, ss);
             }
           }
         }
-        qss[(t * kTransformWG + wg) * kTile + row] = ss;
+        qss[(t * C::kTWG + wg) * kTile + row] = ss;
       }
     }
     // every transform thread arrives, also one whose wait gave up
-    ok = named_barrier_and(1, 32 * kTransformWarps, ok);
+    ok = named_barrier_and(1, 32 * C::kTW, ok);
     if (ok) {
-      const float m1 = fmaxf(sqrtf(qss[row] + qss[kTile + row]), 1e-12f);
+      float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+      for (int g = 0; g < C::kTWG; ++g) {
+        s1 += qss[g * kTile + row];
+        if constexpr (DIFF) s2 += qss[(C::kTWG + g) * kTile + row];
+      }
+      const float m1 = fmaxf(sqrtf(s1), 1e-12f);
       c.rq1 = 1.0f / m1;
       c.tq1 = tau * m1;
       if constexpr (DIFF) {
-        const float m2 = fmaxf(sqrtf(qss[2 * kTile + row] + qss[3 * kTile + row]), 1e-12f);
+        const float m2 = fmaxf(sqrtf(s2), 1e-12f);
         c.rq2 = lam2 / m2;
         c.tq2 = tau * m2;
       }
@@ -499,9 +548,9 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     if (!ok) break;
     tc_fence_after();
     const uint32_t s1col = C::col_s(slot);
-    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>>(
+    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>, F16, kChunks>(
         tmem + lane_off, s1col, C::kColS2, wg, rk_s + re * C::kRkPerTile, grow - j * kTile, j >= qt, c,
-        p.relu_power, c.lam, [&] {
+        p.relu_power, c.lam, p.p_scale, [&] {
           // S2 is in registers: hand its TMEM slot back so QK2 of the next
           // tile runs on the tensor cores while this tile is transformed
           tc_fence_before();
@@ -544,31 +593,40 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
   uint8_t* stage = smem + C::kOffRing;
   if (ok) {
     tc_fence_after();
-    constexpr int kCols = D / kTransformWG;
-    static_assert(kCols % 32 == 0, "epilogue reads 32-column chunks");
+    constexpr int kCols = D / C::kTWG;                 // output columns of this warpgroup
+    constexpr int kPiece = kCols < 32 ? kCols : 32;    // columns per TMEM load
+    static_assert(kCols % kPiece == 0 && kPiece % 16 == 0, "epilogue reads 16- or 32-column pieces");
     uint8_t* srow = stage + row * 128;
     const uint32_t sw = static_cast<uint32_t>(row & 7);
 #pragma unroll
-    for (int c0 = 0; c0 < kCols; c0 += 32) {
+    for (int c0 = 0; c0 < kCols; c0 += kPiece) {
       const int col = wg * kCols + c0;
-      uint32_t o[32];
-      tmem_ld32(tmem + lane_off + C::kColO + col, o);
+      uint32_t o[kPiece];
+      if constexpr (kPiece == 32)
+        tmem_ld32(tmem + lane_off + C::kColO + col, o);
+      else
+        tmem_ld16(tmem + lane_off + C::kColO + col, o);
       tmem_wait_ld();
+      if constexpr (F16) {
+#pragma unroll
+        for (int t = 0; t < kPiece; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * p.o_unscale);
+      }
       if (p.out_f32) {
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
+        for (int t = 0; t < kPiece / 4; ++t) {
           const int c = col + 4 * t;  // box c / 32, 16-B chunk (c % 32) / 4
           *reinterpret_cast<uint4*>(srow + (c >> 5) * C::kBoxBytes + ((((c & 31) >> 2) ^ sw) << 4)) =
               make_uint4(o[4 * t], o[4 * t + 1], o[4 * t + 2], o[4 * t + 3]);
         }
       } else {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kPiece / 8; ++t) {
           const int c = col + 8 * t;  // box c / 64, 16-B chunk (c % 64) / 8
           uint32_t w[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h)
-            w[h] = pack_bf16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]));
+            w[h] = F16 ? pack_f16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]))
+                       : pack_bf16x2(__uint_as_float(o[8 * t + 2 * h]), __uint_as_float(o[8 * t + 2 * h + 1]));
           *reinterpret_cast<uint4*>(srow + (c >> 6) * C::kBoxBytes + ((((c & 63) >> 3) ^ sw) << 4)) =
               make_uint4(w[0], w[1], w[2], w[3]);
         }
@@ -576,7 +634,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     }
     fence_proxy_async_smem();
   }
-  ok = named_barrier_and(2, 32 * kTransformWarps, ok);
+  ok = named_barrier_and(2, 32 * C::kTW, ok);
   if (ok && warp == 2 && lane == 0) {
     const int n_boxes = p.out_f32 ? D / 32 : D / 64;
     const int box_cols = p.out_f32 ? 32 : 64;
@@ -586,8 +644,8 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
   }
 }
 
-template <int D, bool DIFF, bool NORM, bool POS, int PM>
-__global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
+template <int D, bool DIFF, bool NORM, bool POS, int PM, bool F16>
+__global__ void __maxnreg__((Cfg<D, DIFF>::kMaxRegs)) tda_tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
   using C = Cfg<D, DIFF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -617,13 +675,14 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
     mbar_init(&bars->drain2, 1);
     for (int i = 0; i < 3; ++i) {
       mbar_init(&bars->s_full[i], DIFF ? 2 : 1);
-      mbar_init(&bars->p_full[i], kTransformWarps);
+      mbar_init(&bars->p_full[i], C::kTW);
+      mbar_init(&bars->pv_done[i], 1);
       bars->tile_mask[i] = 0;
     }
-    for (int i = 0; i < 2; ++i) mbar_init(&bars->s2_free[i], kTransformWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(&bars->s2_free[i], C::kTW);
     for (int i = 0; i < kRkRing; ++i) {
       mbar_init(&bars->rk_full[i], 1);
-      mbar_init(&bars->rk_empty[i], kTransformWarps);
+      mbar_init(&bars->rk_empty[i], C::kTW);
     }
     for (int i = 0; i < C::kSlots; ++i) {
       mbar_init(&bars->slot_full[i], 1);
@@ -648,12 +707,17 @@ __global__ void __maxnreg__(168) tda_tc_fwd_kernel(const __grid_constant__ TcFwd
     if (lane == 0) run_producer<D, DIFF, NORM>(p, smem, bars, ctl, bh, qt, n_kt);
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) run_mma<D, DIFF>(smem, bars, ctl, tmem, n_kt);
+    if (lane == 0) run_mma<D, DIFF, F16>(smem, bars, ctl, tmem, n_kt);
     __syncwarp();
-  } else if (warp < kQk2Warp) {
-    run_transform<D, DIFF, NORM, POS, PM>(p, smem, bars, ctl, tmem, bh, qt, n_kt, warp, lane);
-  } else if constexpr (DIFF) {
-    if (lane == 0) run_mma_qk2<D>(smem, bars, ctl, tmem, n_kt);
+  } else if (warp < C::kQk2W) {
+    run_transform<D, DIFF, NORM, POS, PM, F16>(p, smem, bars, ctl, tmem, bh, qt, n_kt, warp, lane);
+  } else if (warp == C::kQk2W) {
+    if (lane == 0) {
+      if constexpr (DIFF)
+        run_mma_qk2<D, F16>(smem, bars, ctl, tmem, n_kt);
+      else
+        run_mma_qk<D, F16>(smem, bars, ctl, tmem, n_kt);
+    }
     __syncwarp();
   }
 
@@ -708,8 +772,6 @@ struct PCfg {
   static __device__ __forceinline__ uint32_t col_s(int slot) {
     return DIFF ? (slot ? 256u : 0u) : static_cast<uint32_t>(slot * 128);
   }
-  static constexpr uint32_t kIdescQK = idesc_f16(128, 128, true, false);
-  static constexpr uint32_t kIdescPV = idesc_f16(128, D, true, true);
   // ring entries per key tile: K and V (rect); K1, K2, V (diff)
   static constexpr int kLoadsPerTile = DIFF ? 3 : 2;
 };
@@ -1111,9 +1173,9 @@ __device__ void p_transform(const TcFwdParams& p, uint8_t* smem, PBars* bars, co
     const int slot = G % C::kSSlots;
     if (!mbar_wait_warp(&bars->s_full[slot], (G / C::kSSlots) & 1, ctl, ST_TR_S)) return false;
     tc_fence_after();
-    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>>(
+    const uint32_t nz = transform_tile<PM, DIFF, NORM, POS, kRollChunks<DIFF>, kRollHalves<DIFF>, false, kChunks>(
         tmem + lane_off, C::col_s(slot), C::kColS2, wg, rk_s + re * C::kRkPerTile, qt * kTile + row - j * kTile,
-        j >= qt, c, p.relu_power, c.lam, [&] {
+        j >= qt, c, p.relu_power, c.lam, 1.0f, [&] {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&bars->s2_free[G & 1]);
@@ -1344,11 +1406,13 @@ cudaError_t launch_persistent(const TcFwdParams& p, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-template <int D, bool DIFF, bool NORM, bool POS, int PM>
+template <int D, bool DIFF, bool NORM, bool POS, int PM, bool F16>
 cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
-  if (p.item_ctr) return launch_persistent<D, DIFF, NORM, POS, PM>(p, stream);
+  if constexpr (!F16) {
+    if (p.item_ctr) return launch_persistent<D, DIFF, NORM, POS, PM>(p, stream);
+  }
   using C = Cfg<D, DIFF>;
-  auto kern = tda_tc_fwd_kernel<D, DIFF, NORM, POS, PM>;
+  auto kern = tda_tc_fwd_kernel<D, DIFF, NORM, POS, PM, F16>;
   static bool attr_done = false;  // per instantiation; attribute is per-function, idempotent
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
@@ -1356,7 +1420,7 @@ cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
     attr_done = true;
   }
   const unsigned grid = static_cast<unsigned>(p.BH) * static_cast<unsigned>(p.n_qtiles);
-  constexpr int kThreads = threads_for<DIFF>();
+  constexpr int kThreads = C::kThreads;
   kern<<<grid, kThreads, C::kSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e == cudaErrorLaunchOutOfResources) {
@@ -1374,28 +1438,34 @@ cudaError_t launch_one(const TcFwdParams& p, cudaStream_t stream) {
   return e;
 }
 
-template <int D, bool DIFF, bool NORM, bool POS>
+template <int D, bool DIFF, bool NORM, bool POS, bool F16 = false>
 cudaError_t dispatch_pow(const TcFwdParams& p, int pm, cudaStream_t s) {
   switch (pm) {
-    case POW_1: return launch_one<D, DIFF, NORM, POS, POW_1>(p, s);
-    case POW_2: return launch_one<D, DIFF, NORM, POS, POW_2>(p, s);
-    case POW_3: return launch_one<D, DIFF, NORM, POS, POW_3>(p, s);
-    default: return launch_one<D, DIFF, NORM, POS, POW_GENERAL>(p, s);
+    case POW_1: return launch_one<D, DIFF, NORM, POS, POW_1, F16>(p, s);
+    case POW_2: return launch_one<D, DIFF, NORM, POS, POW_2, F16>(p, s);
+    case POW_3: return launch_one<D, DIFF, NORM, POS, POW_3, F16>(p, s);
+    default: return launch_one<D, DIFF, NORM, POS, POW_GENERAL, F16>(p, s);
   }
 }
 
 // beta >= 0 (tau >= 0): zero halves are recognised from the raw scores, and
 // with normalize the ReLU is a saturating multiply
 template <int D, bool DIFF>
-cudaError_t dispatch_norm(const TcFwdParams& p, bool norm, int pm, cudaStream_t s) {
+cudaError_t dispatch_norm(const TcFwdParams& p, bool norm, int pm, bool fp16, cudaStream_t s) {
+  if (fp16) {
+    // fp16 operands: normalized scores only (P bounded, see the launcher)
+    if (!norm) return cudaErrorInvalidValue;
+    return p.causal_skip ? dispatch_pow<D, DIFF, true, true, true>(p, pm, s)
+                         : dispatch_pow<D, DIFF, true, false, true>(p, pm, s);
+  }
   if (norm)
     return p.causal_skip ? dispatch_pow<D, DIFF, true, true>(p, pm, s) : dispatch_pow<D, DIFF, true, false>(p, pm, s);
   return p.causal_skip ? dispatch_pow<D, DIFF, false, true>(p, pm, s) : dispatch_pow<D, DIFF, false, false>(p, pm, s);
 }
 
 template <int D>
-cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, cudaStream_t s) {
-  return diff ? dispatch_norm<D, true>(p, norm, pm, s) : dispatch_norm<D, false>(p, norm, pm, s);
+cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, bool fp16, cudaStream_t s) {
+  return diff ? dispatch_norm<D, true>(p, norm, pm, fp16, s) : dispatch_norm<D, false>(p, norm, pm, fp16, s);
 }
 
 }  // namespace
@@ -1408,13 +1478,17 @@ cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, cu
 // word with a running one, which would then skip work items.
 __device__ unsigned g_item_ctr[1024];
 
-static bool use_persistent_forward(bool differential, int head_dim, int n_qtiles) {
-  static const int forced = [] {
+// Kernel choice.  The one-CTA-per-tile kernel is the default: with its PV and
+// QK products issued from separate threads it measured 0.501 ms at rect bf16
+// (4,32,4096,128) against 0.524 ms for the persistent kernel, equal at
+// (4,32,2048,128), and ahead at S = 8192 and for the differential form.
+// TDA_B200_FWD_PERSISTENT=1 selects the persistent kernel (=0 or unset: not).
+static bool use_persistent_forward(bool /*differential*/, int /*head_dim*/, int /*n_qtiles*/) {
+  static const bool forced = [] {
     const char* v = std::getenv("TDA_B200_FWD_PERSISTENT");
-    return (v && v[0] == '1') ? 1 : ((v && v[0] == '0') ? 0 : -1);
+    return v && v[0] == '1';
   }();
-  if (forced >= 0) return forced == 1;
-  return !differential && head_dim == 128 && n_qtiles <= 32;
+  return forced;
 }
 
 // Device address of g_item_ctr on the current device, looked up once per
@@ -1446,15 +1520,15 @@ static cudaError_t prepare_item_counter(TcFwdParams& p, cudaStream_t stream) {
 }
 
 cudaError_t launch_tc_fwd(const TcFwdParams& p_in, int head_dim, bool differential, bool normalize, int pow_mode,
-                          cudaStream_t stream) {
+                          bool fp16, cudaStream_t stream) {
   TcFwdParams p = p_in;
   p.item_ctr = nullptr;
-  if (use_persistent_forward(differential, head_dim, p.n_qtiles)) {
+  if (!fp16 && use_persistent_forward(differential, head_dim, p.n_qtiles)) {
     cudaError_t e = prepare_item_counter(p, stream);
     if (e != cudaSuccess) return e;
   }
-  if (head_dim == 128) return dispatch_diff<128>(p, differential, normalize, pow_mode, stream);
-  if (head_dim == 64) return dispatch_diff<64>(p, differential, normalize, pow_mode, stream);
+  if (head_dim == 128) return dispatch_diff<128>(p, differential, normalize, pow_mode, fp16, stream);
+  if (head_dim == 64) return dispatch_diff<64>(p, differential, normalize, pow_mode, fp16, stream);
   return cudaErrorInvalidValue;
 }
 

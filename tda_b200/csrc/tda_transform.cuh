@@ -121,11 +121,14 @@ __device__ __forceinline__ float2 pow2v(float2 u, float p) {
 // instruction cache at the cost of the register moves.  rk1/rk2: this chunk's 32 inverse key norms; rkm1/rkm2:
 // the maxima of its two halves.  Returns this lane's 2-bit mask of halves
 // holding a nonzero P.
-template <int PM, bool DIFF, bool NORM, bool POS, bool ROLL>
+// F16: the operands are fp16 (q, k, v), so P is written as fp16 hi + lo of
+// P * pscale (a power of two that keeps P in fp16's normal range; the
+// epilogue divides it out exactly).
+template <int PM, bool DIFF, bool NORM, bool POS, bool ROLL, bool F16 = false>
 __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t (&b)[32], uint32_t s1_addr,
                                                     const float* rk1, const float* rk2, const float* rkm1,
                                                     const float* rkm2, int limit, bool diag, const RowCoef& c,
-                                                    float relu_power, float lam) {
+                                                    float relu_power, float lam, float pscale = 1.0f) {
   constexpr bool kFold = PM != POW_GENERAL;
   constexpr bool SAT = NORM && POS;  // normalized scores minus tau <= 1
   if (diag) {
@@ -259,12 +262,20 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
         } else {
           P = pow2v<PM>(u1, relu_power);
         }
-        // hi = P truncated to bf16 (exact in fp32), lo = bf16(P - hi): hi + lo
-        // carries ~16 significant bits of P.
-        const uint32_t p0 = __float_as_uint(P.x), p1 = __float_as_uint(P.y);
-        hi[q] = __byte_perm(p0, p1, 0x7632);
-        const float2 l = sub2(P, f2u(p0 & 0xFFFF0000u, p1 & 0xFFFF0000u));
-        lo[q] = pack_bf16x2(l.x, l.y);
+        if constexpr (F16) {
+          // hi = fp16(P * pscale), lo = fp16(P * pscale - hi): ~22 bits
+          const float2 t = __fmul2_rn(P, make_float2(pscale, pscale));
+          hi[q] = pack_f16x2(t.x, t.y);
+          const float2 l = sub2(t, unpack_f16x2(hi[q]));
+          lo[q] = pack_f16x2(l.x, l.y);
+        } else {
+          // hi = P truncated to bf16 (exact in fp32), lo = bf16(P - hi): hi + lo
+          // carries ~16 significant bits of P.
+          const uint32_t p0 = __float_as_uint(P.x), p1 = __float_as_uint(P.y);
+          hi[q] = __byte_perm(p0, p1, 0x7632);
+          const float2 l = sub2(P, f2u(p0 & 0xFFFF0000u, p1 & 0xFFFF0000u));
+          lo[q] = pack_bf16x2(l.x, l.y);
+        }
       }
     } else {
 #pragma unroll
@@ -286,8 +297,9 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
   return nz;
 }
 
-// The two 32-key chunks a transform thread owns in one key tile (warpgroup
-// `wg` of two).  TMEM columns: S1 at s1col, S2 at s2col (differential).
+// The 32-key chunks a transform thread owns in one key tile: NCH = 2 (two
+// transform warpgroups; warpgroup `wg` owns chunks 2 wg, 2 wg + 1) or NCH = 1
+// (four warpgroups; chunk wg).  TMEM columns: S1 at s1col, S2 at s2col (differential).
 // rk_tile: the tile's entry of the key-table ring: rk1[128] (rk2[128]) then
 // the per-16-key maxima rkmax1[8] (rkmax2[8]).
 // With the differential form, all of S2 is loaded first and `release_s2()` is
@@ -298,13 +310,30 @@ __device__ __forceinline__ uint32_t transform_chunk(uint32_t (&a)[32], uint32_t 
 // rolled loop (the second chunk's registers are moved into the first's);
 // ROLL_H: likewise for the two halves of a chunk.
 // Returns bit (2 cc + h): 16-key half h of chunk cc holds a nonzero P.
-template <int PM, bool DIFF, bool NORM, bool POS, bool ROLL_C, bool ROLL_H, typename ReleaseS2>
+template <int PM, bool DIFF, bool NORM, bool POS, bool ROLL_C, bool ROLL_H, bool F16, int NCH, typename ReleaseS2>
 __device__ __forceinline__ uint32_t transform_tile(uint32_t tmem_row, uint32_t s1col, uint32_t s2col, int wg,
                                                    const float* rk_tile, int limit0, bool diag, const RowCoef& c,
-                                                   float relu_power, float lam, ReleaseS2&& release_s2) {
+                                                   float relu_power, float lam, float pscale,
+                                                   ReleaseS2&& release_s2) {
+  static_assert(NCH == 1 || NCH == 2, "one or two 32-key chunks per thread");
   constexpr int kMaxOff = DIFF ? 256 : 128;  // rkmax after rk1 (and rk2)
-  const int ch0 = 2 * wg;
+  const int ch0 = NCH * wg;
   uint32_t nz = 0;
+  if constexpr (NCH == 1) {
+    // one 32-key chunk per thread (four transform warpgroups): its S1 (and
+    // S2) columns in one load; S2's TMEM slot is handed back as soon as it
+    // sits in registers
+    uint32_t a[32], b[32];
+    tmem_ld32(tmem_row + s1col + 32 * ch0, a);
+    if constexpr (DIFF) tmem_ld32(tmem_row + s2col + 32 * ch0, b);
+    tmem_wait_ld();
+    if constexpr (DIFF) release_s2();
+    const float* r1 = rk_tile + 32 * ch0;
+    const float* m1 = rk_tile + kMaxOff + 2 * ch0;
+    return transform_chunk<PM, DIFF, NORM, POS, ROLL_H, F16>(a, b, tmem_row + s1col + 32 * ch0, r1, r1 + 128, m1,
+                                                             m1 + 8, limit0 - 32 * ch0, diag, c, relu_power, lam,
+                                                             pscale);
+  }
   uint32_t a[32], b[32], b1[32];
   if constexpr (DIFF) {
     tmem_ld32(tmem_row + s1col + 32 * ch0, a);
@@ -321,8 +350,9 @@ __device__ __forceinline__ uint32_t transform_tile(uint32_t tmem_row, uint32_t s
     const int ch = ch0 + cc;
     const float* r1 = rk_tile + 32 * ch;
     const float* m1 = rk_tile + kMaxOff + 2 * ch;
-    nz |= transform_chunk<PM, DIFF, NORM, POS, ROLL_H>(x, y, tmem_row + s1col + 32 * ch, r1, r1 + 128, m1, m1 + 8,
-                                                       limit0 - 32 * ch, diag, c, relu_power, lam)
+    nz |= transform_chunk<PM, DIFF, NORM, POS, ROLL_H, F16>(x, y, tmem_row + s1col + 32 * ch, r1, r1 + 128, m1,
+                                                            m1 + 8, limit0 - 32 * ch, diag, c, relu_power, lam,
+                                                            pscale)
           << (2 * cc);
   };
   if constexpr (ROLL_C) {

@@ -18,7 +18,8 @@ behaviour:
   exact fp32 on CUDA cores).
 
 Forward data path: CUDA tensors only.  bf16 with head_dim 64/128 runs the
-tcgen05 tensor-core kernel; fp32 with head_dim 64/128 runs the tcgen05 kind::tf32
+tcgen05 tensor-core kernel, and so does fp16 with head_dim 64/128 when
+normalized (fp16 operands; P bounded); fp32 with head_dim 64/128 runs the tcgen05 kind::tf32
 kernel with three TF32 products per fp32 product (fp32 accuracy); fp32 at
 other head dims runs the exact-fp32 CUDA-core kernel; other dtypes / head dims
 are widened to fp32 on the device.  There is no CPU fallback: CPU tensors
@@ -63,9 +64,25 @@ def _scalar(x) -> float:
     return float(x.item()) if isinstance(x, torch.Tensor) else float(x)
 
 
-def _plan(tensors, what: str):
+def _fp16_ok(normalize: bool, beta: float, p: float, S: int, D: int) -> bool:
+    """fp16 operands on the tensor cores need P = relu(z)^p bounded (its fp16
+    hi + lo split): normalize, p > 0 and (1 + max(0, -beta) sqrt(2 ln S / D))^p
+    <= 16384 -- the rule the C library applies (tda_b200.h)."""
+    import math
+    if not normalize or not p > 0.0:
+        return False
+    tau_max = -beta * math.sqrt(2.0 * math.log(S) / D) if beta < 0.0 else 0.0
+    try:
+        return (1.0 + tau_max) ** p <= 16384.0
+    except OverflowError:
+        return False
+
+
+def _plan(tensors, what: str, normalize: bool = False, beta: float = 0.0, p: float = 2.0):
     """Validate device / shape and pick the kernel path.  Returns
-    (kind, compute_tensors, orig_dtype)."""
+    (kind, compute_tensors, orig_dtype): bf16 (head_dim 64 / 128) and fp16
+    (head_dim 64 / 128, normalized, P bounded) run on the tensor cores in
+    their own type; everything else is widened to fp32."""
     t0 = tensors[0]
     for t in tensors:
         if not isinstance(t, torch.Tensor):
@@ -89,10 +106,23 @@ def _plan(tensors, what: str):
         raise ValueError(f"{what}: head_dim must be a power of two in [16, 256], got {D}")
     if common == torch.bfloat16 and D in (64, 128):
         kind, cdt = _lib.TDA_BF16, torch.bfloat16
+    elif common == torch.float16 and D in (64, 128) and _fp16_ok(normalize, beta, p, t0.shape[2], D):
+        kind, cdt = _lib.TDA_F16, torch.float16
     else:
         kind, cdt = _lib.TDA_F32, torch.float32
     comp = [t.to(cdt).contiguous() for t in tensors]
     return kind, comp, orig
+
+
+_KIND_OF = {torch.float32: _lib.TDA_F32, torch.bfloat16: _lib.TDA_BF16, torch.float16: _lib.TDA_F16}
+
+
+def _raw_dtype(kind: int, out_dtype) -> torch.dtype:
+    """Element type the kernel writes: the compute type, or fp32 when asked
+    for (the accumulator of a bf16 / fp16 computation)."""
+    if kind == _lib.TDA_F32 or out_dtype == torch.float32:
+        return torch.float32
+    return torch.float16 if kind == _lib.TDA_F16 else torch.bfloat16
 
 
 def _finish(out: torch.Tensor, orig: torch.dtype, out_dtype) -> torch.Tensor:
@@ -151,7 +181,7 @@ def _diff_lambda_call(ts, strided, kind, out, lam_dev, beta_v, p_v, normalize):
     strides = None
     if strided:
         strides = (ctypes.c_int64 * 15)(*[x for t in ts for x in t.stride()[:3]])
-    out_kind = _lib.TDA_F32 if out.dtype == torch.float32 else _lib.TDA_BF16
+    out_kind = _KIND_OF[out.dtype]
     stream = torch.cuda.current_stream(out.device).cuda_stream
     with torch.cuda.device(out.device):
         rc = lib.tda_diff_fwd_lambda(*[t.data_ptr() for t in ts],
@@ -174,7 +204,7 @@ def _strided_call(entry, ts, out_dtype, extra, normalize, differential):
     ws_n = lib.tda_workspace_size(int(differential), _lib.TDA_BF16, B * H, S, D, int(normalize))
     ws = torch.empty(ws_n, dtype=torch.uint8, device=out.device) if ws_n else None
     strides = (ctypes.c_int64 * (3 * len(ts)))(*[x for t in ts for x in t.stride()[:3]])
-    out_kind = _lib.TDA_F32 if raw_dt == torch.float32 else _lib.TDA_BF16
+    out_kind = _KIND_OF[raw_dt]
     stream = torch.cuda.current_stream(out.device).cuda_stream
     with torch.cuda.device(out.device):
         rc = getattr(lib, entry)(*[t.data_ptr() for t in ts], ctypes.cast(strides, ctypes.c_void_p),
@@ -197,9 +227,9 @@ def rect_forward(q, k, v, beta, relu_power=2.0, normalize: bool = False, out_dty
         # strided views (e.g. (B, S, H, D) transposed) are read in place
         out = _strided_call("tda_rect_fwd_strided", [q, k, v], out_dtype, (beta_v, p_v), normalize, False)
         return _finish(out, q.dtype, out_dtype)
-    kind, (qc, kc, vc), orig = _plan([q, k, v], "threshold_rela_triton")
+    kind, (qc, kc, vc), orig = _plan([q, k, v], "threshold_rela_triton", normalize, beta_v, p_v)
     B, H, S, D = qc.shape
-    raw_dt = torch.float32 if (kind == _lib.TDA_F32 or out_dtype == torch.float32) else torch.bfloat16
+    raw_dt = _raw_dtype(kind, out_dtype)
     out = torch.empty((B, H, S, D), dtype=raw_dt, device=qc.device)
     if out.numel() == 0:
         return _finish(out, orig, out_dtype)
@@ -207,7 +237,7 @@ def rect_forward(q, k, v, beta, relu_power=2.0, normalize: bool = False, out_dty
     ws_n = lib.tda_workspace_size(0, kind, B * H, S, D, int(normalize))
     ws = torch.empty(ws_n, dtype=torch.uint8, device=qc.device) if ws_n else None
     stream = torch.cuda.current_stream(qc.device).cuda_stream
-    out_kind = _lib.TDA_F32 if raw_dt == torch.float32 else _lib.TDA_BF16
+    out_kind = _KIND_OF[raw_dt]
     with torch.cuda.device(qc.device):
         rc = lib.tda_rect_fwd(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), kind, out_kind,
                               B * H, S, D, beta_v, p_v, int(normalize),
@@ -251,9 +281,10 @@ def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normaliz
         out = _strided_call("tda_diff_fwd_strided", [q1, q2, k1, k2, v], out_dtype,
                             (beta_v, _scalar(lambda_param), p_v), normalize, True)
         return _finish(out, q1.dtype, out_dtype)
-    kind, (a, b, c, d, e), orig = _plan([q1, q2, k1, k2, v], "differential_threshold_rela_triton")
+    kind, (a, b, c, d, e), orig = _plan([q1, q2, k1, k2, v], "differential_threshold_rela_triton", normalize, beta_v,
+                                        p_v)
     B, H, S, D = a.shape
-    raw_dt = torch.float32 if (kind == _lib.TDA_F32 or out_dtype == torch.float32) else torch.bfloat16
+    raw_dt = _raw_dtype(kind, out_dtype)
     out = torch.empty((B, H, S, D), dtype=raw_dt, device=a.device)
     if out.numel() == 0:
         return _finish(out, orig, out_dtype)
@@ -265,7 +296,7 @@ def diff_forward(q1, q2, k1, k2, v, beta, lambda_param, relu_power=2.0, normaliz
     ws_n = lib.tda_workspace_size(1, kind, B * H, S, D, int(normalize))
     ws = torch.empty(ws_n, dtype=torch.uint8, device=a.device) if ws_n else None
     stream = torch.cuda.current_stream(a.device).cuda_stream
-    out_kind = _lib.TDA_F32 if raw_dt == torch.float32 else _lib.TDA_BF16
+    out_kind = _KIND_OF[raw_dt]
     with torch.cuda.device(a.device):
         rc = lib.tda_diff_fwd(a.data_ptr(), b.data_ptr(), c.data_ptr(), d.data_ptr(), e.data_ptr(), out.data_ptr(),
                               kind, out_kind, B * H, S, D, beta_v, lam_v, p_v, int(normalize),

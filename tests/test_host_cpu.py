@@ -72,6 +72,14 @@ def test_library_rejects_bad_arguments_without_launching():
     assert rc == _lib.TDA_ERR_INVALID  # misaligned pointer
     with pytest.raises(ValueError):
         _lib.check(_lib.TDA_ERR_INVALID)
+    # fp16 runs on the tensor cores only with normalize (P bounded): refused before any launch
+    rc = lib.tda_rect_fwd(16, 16, 16, 16, _lib.TDA_F16, _lib.TDA_F16, 1, 128, 64, 1.0, 2.0, 0, None, 0, 16, None)
+    assert rc == _lib.TDA_ERR_UNSUPPORTED and b"fp16" in lib.tda_last_error()
+    rc = lib.tda_diff_fwd(16, 16, 16, 16, 16, 16, _lib.TDA_F16, _lib.TDA_F16, 1, 128, 64, -4.0, 0.5, 12.0, 1,
+                          None, 0, 16, None)
+    assert rc == _lib.TDA_ERR_UNSUPPORTED  # (1 + 4 sqrt(2 ln 128 / 64))^12 > 16384
+    assert lib.tda_workspace_size(1, _lib.TDA_F16, 2, 100, 64, 1) == lib.tda_workspace_size(1, _lib.TDA_BF16, 2, 100,
+                                                                                            64, 1)
     # device-lambda entry point: NULL lambda and negative strides are rejected
     rc = lib.tda_diff_fwd_lambda(16, 16, 16, 16, 16, None, 16, _lib.TDA_BF16, _lib.TDA_BF16, 1, 2, 128, 64, 1.0,
                                  None, 0, 1, 2.0, 1, None, 0, 16, None)
