@@ -447,11 +447,11 @@ def make_inputs(name, shard, device, layout="bhsd", dtype="bf16"):
     given head whatever the number of ranks.  layout "bshd" stores each tensor
     as (1, S, heads, D) and returns the (1, heads, S, D) transposed view, the
     layout of a fused QKV projection that the strided entry points read in
-    place; dtype "f32" keeps the same values in fp32."""
+    place; dtype "f32" / "f16" keeps the same values in fp32 / fp16."""
     import torch
     op, B, H, S, D, beta, lam, p, norm = WORKLOADS[name]
     n = 5 if op == "diff" else 3
-    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    tdt = {"f32": torch.float32, "f16": torch.float16}.get(dtype, torch.bfloat16)
     xs = []
     for t in range(n):
         if layout == "bshd":
@@ -493,8 +493,10 @@ def run_tda(args, rank, local, world):
     status = ops._status_word(dev)
     S_pad = (S + 127) // 128 * 128
     f32 = args.dtype == "f32"
+    f16 = args.dtype == "f16"  # fp16 operands on the tensor cores: the call runs its own key pre-pass
     strided = args.layout == "bshd"
-    out = torch.empty((1, n_bh, S, D), dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
+    out = torch.empty((1, n_bh, S, D), dtype=torch.float32 if f32 else (torch.float16 if f16 else torch.bfloat16),
+                      device=dev)
     rk = [torch.zeros(n_bh * S_pad // 16 * 17, dtype=torch.float32, device=dev) for _ in range(2)]  # key tables
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
@@ -502,11 +504,12 @@ def run_tda(args, rank, local, world):
 
     # the fp32 path computes the norms inside its kernel; the strided entries
     # run their key-norm pre-pass inside the call (timed with the main kernel)
-    separate_norms = norm and not f32 and not strided
+    separate_norms = norm and not f32 and not f16 and not strided
     # the strided entries take the key-table workspace; fp32 at head_dim 64 takes
     # the TF32 split copies of its tensor-core path (other fp32 head dims: none)
-    ws_kind = _lib.TDA_F32 if f32 else _lib.TDA_BF16
-    ws_n = lib.tda_workspace_size(int(op == "diff"), ws_kind, n_bh, S, D, int(norm)) if (strided or f32) else 0
+    ws_kind = _lib.TDA_F32 if f32 else (_lib.TDA_F16 if f16 else _lib.TDA_BF16)
+    ws_n = (lib.tda_workspace_size(int(op == "diff"), ws_kind, n_bh, S, D, int(norm))
+            if (strided or f32 or f16) else 0)
     ws = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=dev)
     strides = (ctypes.c_int64 * (3 * len(xs)))(*[st for x in xs for st in x.stride()[:3]])
 
@@ -520,7 +523,16 @@ def run_tda(args, rank, local, world):
                 _lib.check(lib.tda_key_inv_norms(ptr[1], _lib.TDA_BF16, n_bh, S, D, rk[0].data_ptr(), sp))
 
     def launch_main():
-        if f32:
+        if f16:
+            if op == "diff":
+                _lib.check(lib.tda_diff_fwd(*ptr, out.data_ptr(), _lib.TDA_F16, _lib.TDA_F16, n_bh, S, D, beta, lam,
+                                            p, int(norm), ws.data_ptr() if ws_n else None, ws_n,
+                                            status.data_ptr(), sp))
+            else:
+                _lib.check(lib.tda_rect_fwd(*ptr, out.data_ptr(), _lib.TDA_F16, _lib.TDA_F16, n_bh, S, D, beta, p,
+                                            int(norm), ws.data_ptr() if ws_n else None, ws_n, status.data_ptr(),
+                                            sp))
+        elif f32:
             if op == "diff":
                 _lib.check(lib.tda_diff_fwd(*ptr, out.data_ptr(), _lib.TDA_F32, _lib.TDA_F32, n_bh, S, D, beta, lam,
                                             p, int(norm), ws.data_ptr() if ws_n else None, ws_n,
@@ -681,13 +693,15 @@ def run_tda(args, rank, local, world):
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "f32" if f32 else "bf16",
+            "dtype": "f32" if f32 else ("f16" if f16 else "bf16"),
             "data": "synthetic",
             "pct_bf16_peak": None if f32 else value / world / peak,
             "config": {
                 "workload": describe(name) + ((", fp32 inputs (tensor cores, three TF32 products per product; "
                                                "main_kernel_ms includes the split pre-pass)") if tf32 else
-                                              (", fp32 inputs (CUDA-core path)" if f32 else ""))
+                                              (", fp32 inputs (CUDA-core path)" if f32 else
+                                               (", fp16 inputs (tensor cores, fp16 operands; main_kernel_ms "
+                                                "includes the key pre-pass)" if f16 else "")))
                 + (", (B, S, H, D) storage read in place through the strided entry (main_kernel_ms includes "
                    "its key-norm pre-pass)" if strided else ""),
                 "layout": args.layout,
@@ -737,8 +751,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layout", choices=["bhsd", "bshd"], default="bhsd",
                     help="bshd: (B, S, H, D) storage passed as transposed views (strided entry points)")
-    ap.add_argument("--dtype", choices=["bf16", "f32"], default="bf16",
-                    help="f32: fp32 inputs on the exact-fp32 CUDA-core path")
+    ap.add_argument("--dtype", choices=["bf16", "f32", "f16"], default="bf16",
+                    help="f32: fp32 inputs (tensor cores at head_dim 64 / 128, else CUDA cores); f16: fp16 inputs "
+                         "on the tensor cores")
     ap.add_argument("--backward", action="store_true",
                     help="time the backward pass of the workload instead of the forward")
     ap.add_argument("--ref-rows", type=int, default=256, help="query rows per reference-arm step")
