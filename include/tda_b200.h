@@ -148,7 +148,8 @@ size_t tda_bwd_workspace_size(int dtype, int64_t batch_heads, int64_t seq_len, i
  * bf16 inputs with head_dim 64 / 128 run on the tensor cores (tcgen05, bf16
  * operands, P and dA as bf16 hi + lo, fp32 accumulation) and need the
  * workspace (tda_bwd_workspace_size) and a device status word; fp32 inputs and
- * head_dim 16 / 32 run exact fp32 on CUDA cores (workspace and status unused).
+ * head_dim 16 / 32 / 256 run exact fp32 on CUDA cores (workspace and status
+ * unused).
  * dq, dk, dv must not alias the inputs. */
 int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, int dtype, float* dq, float* dk,
                  float* dv, int64_t batch_heads, int64_t seq_len, int64_t head_dim, float beta, float relu_power,

@@ -14,13 +14,15 @@
 // and dK exactly as in the reference; with beta >= 0 they have zero gradient
 // and key / query tiles beyond the diagonal are skipped.
 //
-// Two kernels on a 64 x 64 tile grid, 256 threads as 16 x 16, exact fp32 FFMA
-// (inputs bf16 or fp32, widened in shared memory):
-//   dq kernel   one CTA per (batch, head, 64 query rows), loop over key tiles
-//   dkv kernel  one CTA per (batch, head, 64 keys), loop over query tiles
-// Thread (ty, tx) owns tile rows {ty + 16 i} x columns {tx + 16 c} of the
-// score-like 64 x 64 products and rows {ty + 16 i} x head-dim columns
-// {64 g + 4 tx + t} (D >= 64) or {CPT tx + t} (D < 64) of the accumulators.
+// Two kernels on a BT x BT tile grid (BT = 64; 32 at head_dim 256, where four
+// fp32 64-row tiles would not fit in shared memory), 256 threads as 16 x 16,
+// exact fp32 FFMA (inputs bf16 or fp32, widened in shared memory):
+//   dq kernel   one CTA per (batch, head, BT query rows), loop over key tiles
+//   dkv kernel  one CTA per (batch, head, BT keys), loop over query tiles
+// Thread (ty, tx) owns tile rows {ty + 16 i} x columns {tx + 16 c} (i, c <
+// BT / 16) of the score-like BT x BT products and rows {ty + 16 i} x head-dim
+// columns {64 g + 4 tx + t} (D >= 64) or {CPT tx + t} (D < 64) of the
+// accumulators.
 #include <cuda_bf16.h>
 
 #include "tda_internal.h"
@@ -28,18 +30,20 @@
 namespace tda {
 namespace {
 
-constexpr int BT = 64;               // tile rows (queries or keys)
 constexpr int kThreads = 256;
-constexpr int LDP = BT + 16;         // row stride of the 64 x 64 shared products
 
 template <int D>
 struct BwdCfg {
+  static constexpr int BT = D >= 256 ? 32 : 64;    // tile rows (queries or keys)
+  static constexpr int RPT = BT / 16;              // tile rows (and product columns) per thread
+  static constexpr int LDP = BT + 16;              // row stride of the BT x BT shared products
   static constexpr int LD = D + 4;                 // row stride of the D-wide tiles
   static constexpr int CPT = D / 16;               // accumulator columns per thread
   static constexpr int kTileFloats = BT * LD;
   // 4 D-wide tiles, 2 products, per-row scalars (norm factor, tau) x 2
   static constexpr int kFloats = 4 * kTileFloats + 2 * BT * LDP + 4 * BT;
   static constexpr int kBytes = kFloats * 4;
+  static_assert(kBytes <= 227 * 1024, "backward tiles exceed shared memory");
 };
 
 __device__ __forceinline__ float relu_pow_ref(float z, float p) {
@@ -70,12 +74,12 @@ __device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* src)
                      __uint_as_float(u.y & 0xFFFF0000u));
 }
 
-// rows [r0, r0 + 64) of a (BH, S, D) array -> shared [64][ld] fp32 times
+// rows [r0, r0 + BT) of a (BH, S, D) array -> shared [BT][ld] fp32 times
 // `scale`, zero past S.
 template <int D, typename T>
 __device__ __forceinline__ void load_rows(float* dst, int ld, const T* src, int bh, int r0, int S, float scale) {
   constexpr int V4 = D / 4;
-  for (int idx = threadIdx.x; idx < BT * V4; idx += kThreads) {
+  for (int idx = threadIdx.x; idx < BwdCfg<D>::BT * V4; idx += kThreads) {
     const int r = idx / V4, c4 = idx % V4;
     float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
     if (r0 + r < S) {
@@ -95,23 +99,24 @@ template <int D>
 __device__ __forceinline__ void normalize_rows(float* tile, float* rinv) {
   using C = BwdCfg<D>;
   {
-    // four adjacent lanes per row, D/4 dims each
-    const int row = threadIdx.x >> 2, part = threadIdx.x & 3;
+    // kParts adjacent lanes per row (4 for 64 rows, 8 for 32), D / kParts dims each
+    constexpr int kParts = kThreads / C::BT;
+    const int row = threadIdx.x / kParts, part = threadIdx.x % kParts;
     float ss = 0.f;
 #pragma unroll
-    for (int d = part * (D / 4); d < (part + 1) * (D / 4); d += 4) {
+    for (int d = part * (D / kParts); d < (part + 1) * (D / kParts); d += 4) {
       const float4 x = *reinterpret_cast<const float4*>(tile + row * C::LD + d);
       ss = fmaf(x.x, x.x, ss);
       ss = fmaf(x.y, x.y, ss);
       ss = fmaf(x.z, x.z, ss);
       ss = fmaf(x.w, x.w, ss);
     }
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+#pragma unroll
+    for (int off = 1; off < kParts; off <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if (part == 0) rinv[row] = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < BT * D; idx += kThreads) {
+  for (int idx = threadIdx.x; idx < C::BT * D; idx += kThreads) {
     const int r = idx / D, d = idx % D;
     tile[r * C::LD + d] *= rinv[r];
   }
@@ -119,33 +124,35 @@ __device__ __forceinline__ void normalize_rows(float* tile, float* rinv) {
 
 // a[i][c] = A[ty+16i] . B[tx+16c] and b[i][c] = A2[ty+16i] . B2[tx+16c] over D
 template <int D>
-__device__ __forceinline__ void two_score_tiles(float (&a)[4][4], float (&b)[4][4], const float* A, const float* B,
-                                                const float* A2, const float* B2, int ty, int tx) {
+__device__ __forceinline__ void two_score_tiles(float (&a)[BwdCfg<D>::RPT][BwdCfg<D>::RPT],
+                                                float (&b)[BwdCfg<D>::RPT][BwdCfg<D>::RPT], const float* A,
+                                                const float* B, const float* A2, const float* B2, int ty, int tx) {
   using C = BwdCfg<D>;
+  constexpr int R = C::RPT;
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < R; ++i)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < R; ++c) {
       a[i][c] = 0.f;
       b[i][c] = 0.f;
     }
 #pragma unroll 2
   for (int d = 0; d < D; d += 4) {
-    float4 xa[4], xb[4], ya[4], yb[4];
+    float4 xa[R], xb[R], ya[R], yb[R];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < R; ++i) {
       xa[i] = *reinterpret_cast<const float4*>(A + (ty + 16 * i) * C::LD + d);
       ya[i] = *reinterpret_cast<const float4*>(A2 + (ty + 16 * i) * C::LD + d);
     }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < R; ++c) {
       xb[c] = *reinterpret_cast<const float4*>(B + (tx + 16 * c) * C::LD + d);
       yb[c] = *reinterpret_cast<const float4*>(B2 + (tx + 16 * c) * C::LD + d);
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < R; ++i)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < R; ++c) {
         a[i][c] = fmaf(xa[i].x, xb[c].x, a[i][c]);
         a[i][c] = fmaf(xa[i].y, xb[c].y, a[i][c]);
         a[i][c] = fmaf(xa[i].z, xb[c].z, a[i][c]);
@@ -158,27 +165,28 @@ __device__ __forceinline__ void two_score_tiles(float (&a)[4][4], float (&b)[4][
   }
 }
 
-// acc[i][col] += sum_j M[ty+16i][j] * X[j][col] (M: 64 x 64 at stride LDP, X: 64 x D at stride LD)
+// acc[i][col] += sum_j M[ty+16i][j] * X[j][col] (M: BT x BT at stride LDP, X: BT x D at stride LD)
 template <int D>
-__device__ __forceinline__ void mac_rows(float (&acc)[4][BwdCfg<D>::CPT], const float* M, const float* X, int ty,
-                                         int tx) {
+__device__ __forceinline__ void mac_rows(float (&acc)[BwdCfg<D>::RPT][BwdCfg<D>::CPT], const float* M,
+                                         const float* X, int ty, int tx) {
   using C = BwdCfg<D>;
+  constexpr int R = C::RPT;
 #pragma unroll 2
-  for (int j = 0; j < BT; j += 4) {
-    float4 m4[4];  // four j per 16-byte load of each row of M
+  for (int j = 0; j < C::BT; j += 4) {
+    float4 m4[R];  // four j per 16-byte load of each row of M
 #pragma unroll
-    for (int i = 0; i < 4; ++i) m4[i] = *reinterpret_cast<const float4*>(M + (ty + 16 * i) * LDP + j);
+    for (int i = 0; i < R; ++i) m4[i] = *reinterpret_cast<const float4*>(M + (ty + 16 * i) * C::LDP + j);
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
-      float m[4];
+      float m[R];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) m[i] = jj == 0 ? m4[i].x : (jj == 1 ? m4[i].y : (jj == 2 ? m4[i].z : m4[i].w));
+      for (int i = 0; i < R; ++i) m[i] = jj == 0 ? m4[i].x : (jj == 1 ? m4[i].y : (jj == 2 ? m4[i].z : m4[i].w));
       if constexpr (D >= 64) {
 #pragma unroll
         for (int g = 0; g < D / 64; ++g) {
           const float4 x = *reinterpret_cast<const float4*>(X + (j + jj) * C::LD + 64 * g + 4 * tx);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
+          for (int i = 0; i < R; ++i) {
             acc[i][4 * g + 0] = fmaf(m[i], x.x, acc[i][4 * g + 0]);
             acc[i][4 * g + 1] = fmaf(m[i], x.y, acc[i][4 * g + 1]);
             acc[i][4 * g + 2] = fmaf(m[i], x.z, acc[i][4 * g + 2]);
@@ -190,7 +198,7 @@ __device__ __forceinline__ void mac_rows(float (&acc)[4][BwdCfg<D>::CPT], const 
         for (int t = 0; t < C::CPT; ++t) {
           const float x = X[(j + jj) * C::LD + C::CPT * tx + t];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) acc[i][t] = fmaf(m[i], x, acc[i][t]);
+          for (int i = 0; i < R; ++i) acc[i][t] = fmaf(m[i], x, acc[i][t]);
         }
       }
     }
@@ -234,16 +242,17 @@ __device__ __forceinline__ void store_grad_row(float* dst, float (&acc)[BwdCfg<D
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads) tda_bwd_dq_kernel(const BwdParams p) {
   using C = BwdCfg<D>;
+  constexpr int BT = C::BT, R = C::RPT, LDP = C::LDP;
   extern __shared__ float4 smem_f4[];
   float* sm = reinterpret_cast<float*>(smem_f4);
-  float* Qs = sm;                       // [64][LD] unit (or raw) query rows
-  float* Gs = Qs + C::kTileFloats;      // [64][LD] scaled dout rows
-  float* Ks = Gs + C::kTileFloats;      // [64][LD]
-  float* Vs = Ks + C::kTileFloats;      // [64][LD]
-  float* As = Vs + C::kTileFloats;      // [64][LDP] dA
-  float* rq = As + 2 * BT * LDP;        // [64]
-  float* tau = rq + BT;                 // [64]
-  float* rk = tau + BT;                 // [64]
+  float* Qs = sm;                       // [BT][LD] unit (or raw) query rows
+  float* Gs = Qs + C::kTileFloats;      // [BT][LD] scaled dout rows
+  float* Ks = Gs + C::kTileFloats;      // [BT][LD]
+  float* Vs = Ks + C::kTileFloats;      // [BT][LD]
+  float* As = Vs + C::kTileFloats;      // [BT][LDP] dA
+  float* rq = As + 2 * BT * LDP;        // [BT]
+  float* tau = rq + BT;                 // [BT]
+  float* rk = tau + BT;                 // [BT]
 
   const int n_t = (p.S + BT - 1) / BT;
   const int bh = blockIdx.x % p.BH;
@@ -265,9 +274,9 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dq_kernel(const BwdParams p)
   __syncthreads();
   if (p.normalize) normalize_rows<D>(Qs, rq);
 
-  float acc[4][C::CPT];
+  float acc[R][C::CPT];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < R; ++i)
 #pragma unroll
     for (int t = 0; t < C::CPT; ++t) acc[i][t] = 0.f;
 
@@ -281,13 +290,13 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dq_kernel(const BwdParams p)
       normalize_rows<D>(Ks, rk);
       __syncthreads();
     }
-    float s[4][4], dp[4][4];
+    float s[R][R], dp[R][R];
     two_score_tiles<D>(s, dp, Qs, Ks, Gs, Vs, ty, tx);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < R; ++i) {
       const int r = ty + 16 * i;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < R; ++c) {
         const int cj = tx + 16 * c;
         const float sv = (n0 + cj <= m0 + r) ? s[i][c] : 0.0f;  // causal mask to zero
         As[r * LDP + cj] = dp[i][c] * relu_pow_grad_ref(sv - tau[r], p.relu_power);
@@ -298,7 +307,7 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dq_kernel(const BwdParams p)
   }
 
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < R; ++i) {
     const int r = ty + 16 * i;
     const bool valid = m0 + r < p.S;
     float* dst = p.dq + (static_cast<size_t>(bh) * p.S + (valid ? m0 + r : 0)) * D;
@@ -309,17 +318,18 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dq_kernel(const BwdParams p)
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads) tda_bwd_dkv_kernel(const BwdParams p) {
   using C = BwdCfg<D>;
+  constexpr int BT = C::BT, R = C::RPT, LDP = C::LDP;
   extern __shared__ float4 smem_f4[];
   float* sm = reinterpret_cast<float*>(smem_f4);
-  float* Ks = sm;                       // [64][LD] unit (or raw) key rows
-  float* Vs = Ks + C::kTileFloats;      // [64][LD]
-  float* Qs = Vs + C::kTileFloats;      // [64][LD]
-  float* Gs = Qs + C::kTileFloats;      // [64][LD] scaled dout rows
-  float* Pt = Gs + C::kTileFloats;      // [64 keys][LDP] P^T
-  float* At = Pt + BT * LDP;            // [64 keys][LDP] dA^T
-  float* rk = At + BT * LDP;            // [64]
-  float* tau = rk + BT;                 // [64]
-  float* rq = tau + BT;                 // [64]
+  float* Ks = sm;                       // [BT][LD] unit (or raw) key rows
+  float* Vs = Ks + C::kTileFloats;      // [BT][LD]
+  float* Qs = Vs + C::kTileFloats;      // [BT][LD]
+  float* Gs = Qs + C::kTileFloats;      // [BT][LD] scaled dout rows
+  float* Pt = Gs + C::kTileFloats;      // [BT keys][LDP] P^T
+  float* At = Pt + BT * LDP;            // [BT keys][LDP] dA^T
+  float* rk = At + BT * LDP;            // [BT]
+  float* tau = rk + BT;                 // [BT]
+  float* rq = tau + BT;                 // [BT]
 
   const int n_t = (p.S + BT - 1) / BT;
   const int bh = blockIdx.x % p.BH;
@@ -338,9 +348,9 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dkv_kernel(const BwdParams p
   __syncthreads();
   if (p.normalize) normalize_rows<D>(Ks, rk);
 
-  float dk[4][C::CPT], dv[4][C::CPT];
+  float dk[R][C::CPT], dv[R][C::CPT];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < R; ++i)
 #pragma unroll
     for (int t = 0; t < C::CPT; ++t) {
       dk[i][t] = 0.f;
@@ -361,13 +371,13 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dkv_kernel(const BwdParams p
       __syncthreads();
     }
     // rows = keys (ty + 16 i), columns = queries (tx + 16 c)
-    float s[4][4], dp[4][4];
+    float s[R][R], dp[R][R];
     two_score_tiles<D>(s, dp, Ks, Qs, Vs, Gs, ty, tx);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < R; ++i) {
       const int rj = ty + 16 * i;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < R; ++c) {
         const int ci = tx + 16 * c;
         const bool in_seq = m0 + ci < p.S;
         const float sv = (n0 + rj <= m0 + ci) ? s[i][c] : 0.0f;  // causal mask to zero
@@ -383,7 +393,7 @@ __global__ void __launch_bounds__(kThreads) tda_bwd_dkv_kernel(const BwdParams p
   }
 
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < R; ++i) {
     const int r = ty + 16 * i;
     const bool valid = n0 + r < p.S;
     const size_t off = (static_cast<size_t>(bh) * p.S + (valid ? n0 + r : 0)) * D;
@@ -401,7 +411,7 @@ cudaError_t launch_bwd_d(const BwdParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kBytes);
   if (e != cudaSuccess) return e;
-  const int n_t = (p.S + BT - 1) / BT;
+  const int n_t = (p.S + C::BT - 1) / C::BT;
   const unsigned grid = static_cast<unsigned>(p.BH) * static_cast<unsigned>(n_t);
   kq<<<grid, kThreads, C::kBytes, stream>>>(p);
   e = cudaGetLastError();
@@ -417,6 +427,7 @@ cudaError_t launch_bwd_t(const BwdParams& p, int head_dim, cudaStream_t stream) 
     case 32: return launch_bwd_d<32, T>(p, stream);
     case 64: return launch_bwd_d<64, T>(p, stream);
     case 128: return launch_bwd_d<128, T>(p, stream);
+    case 256: return launch_bwd_d<256, T>(p, stream);
     default: return cudaErrorInvalidValue;
   }
 }

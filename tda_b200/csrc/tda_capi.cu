@@ -549,8 +549,8 @@ int tda_rect_bwd(const void* q, const void* k, const void* v, const void* dout, 
     return fail(TDA_ERR_INVALID, "batch_heads and seq_len must be >= 1 (got %lld, %lld)",
                 static_cast<long long>(batch_heads), static_cast<long long>(seq_len));
   if (dtype != TDA_F32 && dtype != TDA_BF16) return fail(TDA_ERR_INVALID, "dtype must be TDA_F32 or TDA_BF16");
-  if (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128)
-    return fail(TDA_ERR_UNSUPPORTED, "backward supports head_dim 16, 32, 64 or 128 (got %lld)",
+  if (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(TDA_ERR_UNSUPPORTED, "backward supports head_dim 16, 32, 64, 128 or 256 (got %lld)",
                 static_cast<long long>(head_dim));
   if (seq_len > (1ll << 30)) return fail(TDA_ERR_INVALID, "seq_len too large (%lld)", static_cast<long long>(seq_len));
   if (batch_heads * ((seq_len + 63) / 64) > 0x7fffffffll)

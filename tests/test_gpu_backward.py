@@ -2,7 +2,7 @@
 to the reference's own gradients (tests/test_oracle_golden_bwd.py).
 
 Paths and tolerances (rel-L2):
-  * fp32 inputs (and head_dim 16 / 32): exact fp32 on CUDA cores,
+  * fp32 inputs (and head_dim 16 / 32 / 256): exact fp32 on CUDA cores,
     fp32 gradients vs the fp64 oracle                                <= 1e-5
   * bf16 inputs, head_dim 64 / 128: tcgen05 tensor cores, bf16 operands with
     P and dA as bf16 hi + lo, fp32 accumulation; fp32 gradients
@@ -75,11 +75,12 @@ def test_golden_backward_through_autograd(case):
         assert O.rel_l2(_np(g_ours), a[name]) <= 5e-5, (name, O.rel_l2(_np(g_ours), a[name]))
 
 
-@pytest.mark.parametrize("D", [16, 32, 64, 128])
+@pytest.mark.parametrize("D", [16, 32, 64, 128, 256])
 @pytest.mark.parametrize("beta,p,norm", [(1.0, 2.0, True), (0.5, 3.0, False), (-0.5, 2.0, True),
                                          (1.5, 1.0, True), (2.0, 1.5, False)])
 def test_rect_backward_fp32_tiles(D, beta, p, norm):
-    """Several 64-row tiles, a ragged last tile, both tile loops, every head dim."""
+    """Several 64-row tiles (32-row at head_dim 256), a ragged last tile, both
+    tile loops, every head dim."""
     q, k, v, g = _gen(100 + D, 4, (1, 2, 200, D))
     dq, dk, dv = tda_b200.rect_backward(*(x.to(DEV) for x in (q, k, v, g)), beta, p, norm)
     ref = O.rect_bwd(q.numpy(), k.numpy(), v.numpy(), g.numpy(), beta, p, norm)
@@ -102,6 +103,24 @@ def test_rect_backward_bf16_inputs(D):
     for got, r in zip((qg.grad, kg.grad, vg.grad), ref):
         assert got.dtype == torch.bfloat16
         assert O.rel_l2(_np(got), O.bf16_round(r)) <= TOL_BF16
+
+
+def test_head_dim_256_backward_through_autograd():
+    """head_dim 256 (the reference's kernels take any power-of-two BLOCK_D,
+    :368, :436-460): bf16 inputs through the differential form's autograd on
+    the CUDA-core kernels with 32-row tiles, exact fp32 gradients of the bf16
+    values, handed back in bf16."""
+    xs = _gen(700, 6, (1, 2, 150, 256), dtype=torch.bfloat16)
+    ins = [x.to(DEV).requires_grad_(True) for x in xs[:5]]
+    lam = torch.tensor(0.4, device=DEV, requires_grad=True)
+    out = tda_b200.differential_threshold_rela_triton(*ins, 0.5, lam, 2.0, True)
+    out.backward(xs[5].to(DEV))
+    ref = O.diff_bwd(*[x.float().numpy() for x in xs[:5]], xs[5].float().numpy(), 0.5, 0.4, 2.0, True)
+    for got, r in zip(ins, ref[:5]):
+        assert got.grad.dtype == torch.bfloat16
+        assert O.rel_l2(_np(got.grad), O.bf16_round(r)) <= TOL_BF16
+    assert abs(float(lam.grad) - ref[5]) <= 1e-3 * max(1.0, abs(ref[5]))
+    tda_b200.check_status()
 
 
 def test_diff_backward_per_head_lambda():
