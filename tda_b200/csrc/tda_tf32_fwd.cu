@@ -22,8 +22,11 @@
 // (head_dim 64) or 32 (head_dim 128); layout per head_dim in TfCfg below.  At 64:
 //   warp 0  TMA producer: Q h/l once per branch, K h/l and V^T h/l rings of
 //           two entries each (K released by QK, V by PV)
-//   warp 1  MMA issuer (one thread): S = Q K^T (3 x 8 MMAs of M128 N64 K8)
-//           into one of two TMEM S slots; P V^T (3 x 8 MMAs, P from TMEM)
+//   warp 1  PV issuer (one thread): P V^T (3 x 8 MMAs, P from TMEM) per tile
+//   last warp  QK issuer (one thread): S = Q K^T (3 x 8 MMAs of M128 N64 K8)
+//           into one of two TMEM S slots, once the PV reading the slot has run
+//           (two issuing threads, so that one's waits and commits overlap the
+//           other's MMAs)
 //   warps 2-5  transform: thread = query row = TMEM lane; S -> P, written back
 //           as P_h over S and P_l beside it; adds each tile's P V^T into
 //           fp32 registers; epilogue O -> out.
@@ -57,7 +60,8 @@ struct TfCfg {
   static constexpr int kWG = D == 64 ? 1 : 2;           // transform warpgroups
   static constexpr int kVSlots = D == 64 ? 2 : 1;
   static constexpr int kOSlots = D == 64 ? 2 : 1;
-  static constexpr int kThreads = 64 + 128 * kWG;
+  static constexpr int kQkWarp = 2 + 4 * kWG;           // the QK issuer, after the transform warps
+  static constexpr int kThreads = 64 + 128 * kWG + 32;
   static constexpr int kCB = D / 32;                    // 128-byte column boxes of a D-wide row
   static constexpr int kQBytes = kCB * 2 * kBox64;      // 128 rows: two 64-row boxes per column box
   static constexpr int kKBytes = kCB * kBN * 128;       // one K tile (high or low part)
@@ -80,7 +84,8 @@ struct TfCfg {
 constexpr int ST_TF_PROD = 0x601, ST_TF_MMA = 0x602, ST_TF_TR = 0x603, ST_TF_DRAIN = 0x604;
 
 struct Tf32Bars {
-  uint64_t q_full, q_empty, drain;
+  uint64_t q_full, q_empty, drain, drain2;
+  uint64_t pv_done[2];            // per S slot: the PV reading P from it has run
   uint64_t o_full[2], o_free[2];  // per-tile partial O: written by PV, read by the transform
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2];
@@ -307,9 +312,11 @@ __device__ void tf_producer(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, 
   }
 }
 
+// QK issuer (last warp): S = Q K^T into S slot t % 2.  QK_{t+2} waits until
+// PV_t, which reads P_t from the same slot, has run (pv_done).
 template <int D>
-__device__ void tf_mma(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const WaitCtl& ctl, uint32_t tmem,
-                       int n_kt) {
+__device__ void tf_mma_qk(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const WaitCtl& ctl, uint32_t tmem,
+                          int n_kt) {
   using C = TfCfg<D>;
   const int T = p.n_br * n_kt;
   const uint32_t qh = smem_u32(smem + C::kOffQh), ql = smem_u32(smem + C::kOffQl);
@@ -322,6 +329,7 @@ __device__ void tf_mma(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const
       tc_fence_after();
     }
     if (!(ok = mbar_wait(&b->k_full[e], u & 1, ctl, ST_TF_MMA))) return;
+    if (t >= 2 && !(ok = mbar_wait(&b->pv_done[e], (u - 1) & 1, ctl, ST_TF_MMA))) return;
     tc_fence_after();
     const uint32_t kh = smem_u32(smem + C::kOffK + e * 2 * C::kKBytes), kl = kh + C::kKBytes;
     const uint32_t d = tmem + col_s<C::kBN>(e);
@@ -342,16 +350,30 @@ __device__ void tf_mma(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const
     tc_commit(&b->s_full[e]);
     if (j == n_kt - 1 && br + 1 < p.n_br) tc_commit(&b->q_empty);
   };
-  // Each tile's P V goes into a fresh partial O that the transform threads add
-  // into fp32 registers: the tensor core accumulates one tile's products
-  // instead of the whole key range.
-  auto pv = [&](int t) {
+  for (int t = 0; t < T && ok; ++t) qk(t);
+  if (!ok) {  // let every MMA this thread issued finish before TMEM is freed
+    tc_commit(&b->drain2);
+    tf_drain_wait(&b->drain2, 0, ctl);
+  }
+}
+
+// PV issuer (warp 1).  Each tile's P V goes into a fresh partial O that the
+// transform threads add into fp32 registers: the tensor core accumulates one
+// tile's products instead of the whole key range.  The V^T slot is acquired
+// before the wait for P (its load does not depend on P).
+template <int D>
+__device__ void tf_mma_pv(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const WaitCtl& ctl, uint32_t tmem,
+                          int n_kt) {
+  using C = TfCfg<D>;
+  const int T = p.n_br * n_kt;
+  bool ok = true;
+  for (int t = 0; t < T && ok; ++t) {
     const int e = t & 1, u = t >> 1;
     const int ev = t % C::kVSlots, uv = t / C::kVSlots;
     const int eo = t % C::kOSlots, uo = t / C::kOSlots;
-    if (!(ok = mbar_wait(&b->v_full[ev], uv & 1, ctl, ST_TF_MMA))) return;
-    if (!(ok = mbar_wait(&b->p_full[e], u & 1, ctl, ST_TF_MMA))) return;
-    if (uo > 0 && !(ok = mbar_wait(&b->o_free[eo], (uo - 1) & 1, ctl, ST_TF_MMA))) return;
+    if (!(ok = mbar_wait(&b->v_full[ev], uv & 1, ctl, ST_TF_MMA))) break;
+    if (!(ok = mbar_wait(&b->p_full[e], u & 1, ctl, ST_TF_MMA))) break;
+    if (uo > 0 && !(ok = mbar_wait(&b->o_free[eo], (uo - 1) & 1, ctl, ST_TF_MMA))) break;
     tc_fence_after();
     const uint32_t vh = smem_u32(smem + C::kOffV + ev * 2 * C::kVBytes), vl = vh + C::kVBytes;
     const uint32_t d = tmem + C::kColO + 2 * D * eo;
@@ -366,12 +388,7 @@ __device__ void tf_mma(const Tf32FwdParams& p, uint8_t* smem, Tf32Bars* b, const
     }
     tc_commit(&b->v_empty[ev]);
     tc_commit(&b->o_full[eo]);
-  };
-  if (ok) qk(0);
-  if (ok && T > 1) qk(1);
-  for (int t = 0; t < T && ok; ++t) {
-    pv(t);
-    if (ok && t + 2 < T) qk(t + 2);
+    tc_commit(&b->pv_done[e]);
   }
   if (!ok) {  // let every MMA this thread issued finish before TMEM is freed
     tc_commit(&b->drain);
@@ -505,7 +522,9 @@ __global__ void __launch_bounds__(TfCfg<D>::kThreads, 1) tda_tf32_fwd_kernel(con
     mbar_init(&b->q_full, 1);
     mbar_init(&b->q_empty, 1);
     mbar_init(&b->drain, 1);
+    mbar_init(&b->drain2, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&b->pv_done[i], 1);
       mbar_init(&b->k_full[i], 1);
       mbar_init(&b->k_empty[i], 1);
       mbar_init(&b->v_full[i], 1);
@@ -531,7 +550,10 @@ __global__ void __launch_bounds__(TfCfg<D>::kThreads, 1) tda_tf32_fwd_kernel(con
     if (lane == 0) tf_producer<D>(p, smem, b, ctl, bh, m0, n_kt);
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) tf_mma<D>(p, smem, b, ctl, tmem, n_kt);
+    if (lane == 0) tf_mma_pv<D>(p, smem, b, ctl, tmem, n_kt);
+    __syncwarp();
+  } else if (warp == C::kQkWarp) {
+    if (lane == 0) tf_mma_qk<D>(p, smem, b, ctl, tmem, n_kt);
     __syncwarp();
   } else {
     tf_transform<D, PM>(p, b, ctl, tmem, bh, m0, n_kt, warp, lane);
