@@ -56,7 +56,7 @@ constexpr int kQk2Warp = 2 + kTransformWarps;
 template <bool DIFF>
 constexpr int threads_for() { return 32 * (2 + kTransformWarps + (DIFF ? 1 : 0)); }
 constexpr int kRkRing = 4;
-constexpr int kHeadGroup = 4;  // (batch, head) slices interleaved in launch order
+constexpr int kHeadGroup = 2;  // (batch, head) slices interleaved in launch order
 // Transform code layout (instruction-cache footprint versus register moves),
 // chosen per form by measurement: the differential transform is twice the
 // code and runs from one rolled chunk loop (the kernel was instruction-fetch
