@@ -97,17 +97,17 @@ struct View {
 
 View contiguous_view(const void* p, int64_t BH, int64_t S, int64_t D) { return View{p, BH * S * D, S * D, D}; }
 
-// View viewed as 4-D {D, S, heads, batches}; box {64, 128, 1, 1}; 128-B swizzle;
-// 2-byte elements, bf16 or fp16.
+// View viewed as 4-D {D, S, heads, batches}; box {64, box_rows, 1, 1}; 128-B
+// swizzle; 2-byte elements, bf16 or fp16.
 int make_map4(CUtensorMap* m, const View& x, int64_t batches, int64_t heads, int64_t S, int64_t D,
-              bool f16 = false) {
+              bool f16 = false, int box_rows = tda::kTile) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(TDA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(heads),
                         static_cast<cuuint64_t>(batches)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(x.ss * 2), static_cast<cuuint64_t>(x.sh * 2),
                            static_cast<cuuint64_t>(x.sb * 2)};
-  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(tda::kTile), 1, 1};
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
                    const_cast<void*>(x.p), dims, strides, box, estr,
@@ -204,6 +204,10 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
   if (differential) {
     if ((e = make_map4(&prm.tm_q2, q2, batches, heads, S, D, f16))) return e;
     if ((e = make_map4(&prm.tm_k2, k2, batches, heads, S, D, f16))) return e;
+  }
+  if (D == 128) {  // the CTA-pair kernel loads half key tiles (64 rows)
+    if ((e = make_map4(&prm.tm_k1h, k1, batches, heads, S, D, f16, tda::kTile / 2))) return e;
+    if (differential && (e = make_map4(&prm.tm_k2h, k2, batches, heads, S, D, f16, tda::kTile / 2))) return e;
   }
   if ((e = make_out_map(&prm.tm_out, out, out_dtype == TDA_F32, BH, S, D, f16))) return e;
   prm.rk1 = rk1;

@@ -57,6 +57,8 @@ struct TcFwdParams {
   CUtensorMap tm_k2;  // differential only
   CUtensorMap tm_v;
   CUtensorMap tm_out;  // out, contiguous (BH, S, D) as 3-D {D, S, BH}: box {128 B of elements, 128, 1}, 128-B swizzle
+  CUtensorMap tm_k1h;  // head_dim 128: k1 with 64-row boxes (a CTA's half of a key tile, CTA-pair kernel)
+  CUtensorMap tm_k2h;  // same for k2 (differential only)
   const float* rk1;   // key table of k1 (normalize only): rk [BH][S_pad] then rkmax [BH][S_pad/16]
   const float* rk2;   // same for k2 (differential + normalize)
   void* out;          // [BH][S][D], bf16 or f32 (out_f32)
@@ -85,6 +87,9 @@ struct TcFwdParams {
 // fp16 operands, P split into fp16 hi + lo; only with normalize (P bounded).
 cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,
                           bool fp16, cudaStream_t stream);
+// The same forward at head_dim 128 on CTA pairs (tm_k1h / tm_k2h set).
+cudaError_t launch_tc_fwd_pair(const TcFwdParams& p, bool differential, bool normalize, int pow_mode, bool fp16,
+                               cudaStream_t stream);
 
 
 // CUDA-core fp32 forward (exact fp32 FFMA), any power-of-two D in [16, 256].

@@ -342,4 +342,147 @@ __device__ __forceinline__ float fast_ex2(float x) {
   return y;
 }
 
+// ---------------------------------------------------------------- CTA pair
+// Two CTAs of a cluster of two on neighbouring SMs share their tensor-core
+// products (tcgen05 cta_group::2): one thread of the even CTA issues an
+// M = 256 product whose A rows 0-127 come from the even CTA and rows 128-255
+// from the odd one, and whose B columns are split the same way (each CTA
+// holds N/2 of them); each CTA's TMEM receives its own 128 rows.  Every
+// tcgen05 allocation, product and commit of such a kernel is cta_group::2.
+// Addresses of another CTA's shared memory are 32-bit shared::cluster
+// addresses (mapa).
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the object at shared::cta address `a` in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+
+// Every thread of both CTAs arrives; shared-memory writes before it are
+// visible cluster-wide after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier of either CTA, ordering this thread's earlier memory
+// operations (also stores into the other CTA) before the arrival.  The thread
+// waits for the round trip (several hundred ns): for one-off signals only.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait (as mbar_wait) on a local barrier that receives arrivals from
+// the other CTA of the pair: acquire at cluster scope.
+static __device__ __noinline__ bool mbar_wait_cluster_slow(uint32_t bar, uint32_t parity, const WaitCtl& ctl,
+                                                           int code) {
+  const uint64_t t0 = global_timer_ns();
+  uint32_t it = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++it & 31u) == 0) {
+      if (*ctl.abort_flag) return false;
+      const uint64_t waited = global_timer_ns() - t0;
+      if (waited > 1000000ull && *reinterpret_cast<volatile int*>(ctl.status) != ctl.status0) {
+        *ctl.abort_flag = 1;
+        return false;
+      }
+      if (waited > ctl.timeout_ns) {
+        *ctl.abort_flag = 1;
+        atomicCAS(ctl.status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const WaitCtl& ctl, int code) {
+  const uint32_t a = smem_u32(bar);
+  if (mbar_try_wait_cluster(a, parity)) return true;
+  return mbar_wait_cluster_slow(a, parity, ctl, code);
+}
+
+// Asynchronous 4-byte store into the other CTA's shared memory that, once
+// written, completes 4 transaction bytes on an mbarrier there: whoever sees
+// that barrier's phase complete also sees the word.  The issuing thread does
+// not wait for it (unlike an arrive with release at cluster scope, which
+// stalls the thread for the round trip).
+__device__ __forceinline__ void st_async_u32(uint32_t addr_cluster, uint32_t v, uint32_t bar_cluster) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.u32 [%0], %1, [%2];" ::"r"(addr_cluster),
+               "r"(v), "r"(bar_cluster)
+               : "memory");
+}
+
+// 4-D tiled load into this CTA's shared memory whose completion (bytes) is
+// signalled on an mbarrier of either CTA of the pair (the even CTA's, so that
+// the thread issuing the pair's products sees both halves land).
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+// TMEM allocation for the pair: one warp with the same warp index in each CTA
+// issues these; both CTAs receive the same column address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrive once on the mbarrier at `bar_cluster` (either CTA) when every pair
+// product this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+// Pair products, kind::f16: D[tmem] (+)= A * B^T with A from shared memory
+// (ss) or TMEM (ts) and B from shared memory, both CTAs' halves.
+__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 }  // namespace tda

@@ -1519,10 +1519,22 @@ static cudaError_t prepare_item_counter(TcFwdParams& p, cudaStream_t stream) {
   return cudaMemsetAsync(p.item_ctr, 0, sizeof(unsigned), stream);
 }
 
+// CTA-pair kernel (tda_tc_fwd_pair.cu) at head_dim 128: TDA_B200_FWD_PAIR=1
+// selects it, =0 or unset the one-CTA-per-tile kernel.
+static bool use_pair_forward(int head_dim) {
+  static const bool on = [] {
+    const char* v = std::getenv("TDA_B200_FWD_PAIR");
+    return v && v[0] == '1';
+  }();
+  return on && head_dim == 128;
+}
+
 cudaError_t launch_tc_fwd(const TcFwdParams& p_in, int head_dim, bool differential, bool normalize, int pow_mode,
                           bool fp16, cudaStream_t stream) {
   TcFwdParams p = p_in;
   p.item_ctr = nullptr;
+  if (use_pair_forward(head_dim) && !use_persistent_forward(differential, head_dim, p.n_qtiles))
+    return launch_tc_fwd_pair(p, differential, normalize, pow_mode, fp16, stream);
   if (!fp16 && use_persistent_forward(differential, head_dim, p.n_qtiles)) {
     cudaError_t e = prepare_item_counter(p, stream);
     if (e != cudaSuccess) return e;

@@ -11,8 +11,9 @@ seeded) and, in each, 256 query rows (the first 64, the last 64 and 128 spread
 over the sequence).
 
 Each kernel schedule runs in a child process, because the forward kernel
-(one CTA per query tile, or the persistent one-CTA-per-SM kernel) is chosen
-once per process (TDA_B200_FWD_PERSISTENT=0 / 1).
+(one CTA per query tile, the persistent one-CTA-per-SM kernel, or the
+CTA-pair kernel) is chosen once per process (TDA_B200_FWD_PERSISTENT,
+TDA_B200_FWD_PAIR).
 
 Tolerances, as for every bf16 parity test here (rel-L2 over the sampled rows):
   * the kernel's fp32 accumulator output vs the oracle:   <= 1e-3
@@ -132,10 +133,17 @@ def _oracle(name, bhs, rows):
     return np.stack(ref)
 
 
-@pytest.fixture(scope="module", params=["0", "1"], ids=["per_tile", "persistent"])
+SCHEDULES = {
+    "per_tile": {"TDA_B200_FWD_PERSISTENT": "0", "TDA_B200_FWD_PAIR": "0"},
+    "persistent": {"TDA_B200_FWD_PERSISTENT": "1", "TDA_B200_FWD_PAIR": "0"},
+    "pair": {"TDA_B200_FWD_PERSISTENT": "0", "TDA_B200_FWD_PAIR": "1"},
+}
+
+
+@pytest.fixture(scope="module", params=list(SCHEDULES))
 def gpu_results(request, tmp_path_factory):
-    path = str(tmp_path_factory.mktemp("cfg") / f"mode{request.param}.npz")
-    env = dict(os.environ, TDA_B200_FWD_PERSISTENT=request.param)
+    path = str(tmp_path_factory.mktemp("cfg") / f"{request.param}.npz")
+    env = dict(os.environ, **SCHEDULES[request.param])
     subprocess.run([sys.executable, "-c", CHILD, ROOT, ",".join(CONFIGS), path], env=env, check=True,
                    timeout=1200)
     return np.load(path)
