@@ -48,13 +48,13 @@ namespace {
 using namespace tc;
 
 // Persistent kernel: two transform warpgroups (warps 2 .. 9), each thread two
-// 32-key chunks of every key tile; differential form: warp 10 issues the QK2
-// products (second MMA issuer).
+// 32-key chunks of every key tile; warp 10 issues the QK products (rect) or
+// the QK2 products (differential), warp 1 the PV (and QK1) products.
 constexpr int kTransformWG = 2;
 constexpr int kTransformWarps = 4 * kTransformWG;
 constexpr int kQk2Warp = 2 + kTransformWarps;
 template <bool DIFF>
-constexpr int threads_for() { return 32 * (2 + kTransformWarps + (DIFF ? 1 : 0)); }
+constexpr int threads_for() { return 32 * (3 + kTransformWarps); }
 constexpr int kRkRing = 4;
 constexpr int kHeadGroup = 2;  // (batch, head) slices interleaved in launch order
 // Transform code layout (instruction-cache footprint versus register moves),
@@ -785,6 +785,7 @@ struct PBars {
   uint64_t drain2;
   uint64_t s_full[3];
   uint64_t p_full[3];
+  uint64_t pv_done[3];   // rect, per S slot: the PV reading P from it has run
   uint64_t s2_free[2];
   uint64_t rk_full[kRkRing];
   uint64_t rk_empty[kRkRing];
@@ -981,6 +982,10 @@ __device__ __forceinline__ int take_item(PBars* bars, int it, const WaitCtl& ctl
   return got ? idx : -1;
 }
 
+// PV issuer (warp 1), every item in turn: V_j's ring entry is acquired
+// before the wait for P_j.  rect: after PV_j it commits pv_done of P_j's S
+// slot, which hands the slot to the QK issuer (warp 10).  differential: it
+// also issues QK1_{j+2} into P_j's slot right after PV_j.
 template <int D, bool DIFF>
 __device__ void p_mma(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, uint32_t tmem) {
   using C = PCfg<D, DIFF>;
@@ -994,30 +999,19 @@ __device__ void p_mma(const TcFwdParams& p, uint8_t* smem, PBars* bars, const Wa
     int bh, qt;
     decode_item(p, idx, bh, qt);
     const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
-    const int b = DIFF ? 0 : (it & 1);
-    const int use = DIFF ? it : (it >> 1);
-    m.wait(&bars->q_full[b], use & 1, ST_MMA_Q);
-    const uint32_t q1_base = smem_u32(smem + b * C::kQBytes);
     m.o_started = false;
     if constexpr (!DIFF) {
-      int r = base;  // ring order: K0, K1, K2, then per j: V_j, K_{j+3}
-      for (int t = 0; t < C::kSSlots && t < n_kt; ++t) {
-        m.qk(r++, C::col_s((g + t) % C::kSSlots), q1_base);
-        m.commit(&bars->s_full[(g + t) % C::kSSlots]);
-        if (t == n_kt - 1) m.commit(&bars->q_empty[b]);  // the item's last QK
-      }
       for (int j = 0; j < n_kt && m.ok; ++j) {
         const int G = g + j, slot = G % C::kSSlots;
+        const int vslot = m.acquire(base + ring_v_rect(j, n_kt));
         m.wait(&bars->p_full[slot], (G / C::kSSlots) & 1, ST_MMA_P);
         if (j == 0 && it > 0) m.wait(&bars->o_empty, (it - 1) & 1, ST_MMA_O);
-        m.pv(r++, C::col_s(slot), m.slab_mask(G));
-        if (j + C::kSSlots < n_kt) {
-          m.qk(r++, C::col_s(slot), q1_base);
-          m.commit(&bars->s_full[slot]);
-          if (j + C::kSSlots == n_kt - 1) m.commit(&bars->q_empty[b]);
-        }
+        m.pv_at(vslot, C::col_s(slot), m.slab_mask(G));
+        m.commit(&bars->pv_done[slot]);
       }
     } else {
+      m.wait(&bars->q_full[0], it & 1, ST_MMA_Q);
+      const uint32_t q1_base = smem_u32(smem);
       m.qk(base + ring_k1(0), C::col_s(g & 1), q1_base);
       m.commit(&bars->s_full[g & 1]);
       if (n_kt == 1) m.commit(&bars->q_empty[0]);
@@ -1028,9 +1022,10 @@ __device__ void p_mma(const TcFwdParams& p, uint8_t* smem, PBars* bars, const Wa
       }
       for (int j = 0; j < n_kt && m.ok; ++j) {
         const int G = g + j, slot = G & 1;
+        const int vslot = m.acquire(base + ring_v(j, n_kt));
         m.wait(&bars->p_full[slot], (G >> 1) & 1, ST_MMA_P);
         if (j == 0 && it > 0) m.wait(&bars->o_empty, (it - 1) & 1, ST_MMA_O);
-        m.pv(base + ring_v(j, n_kt), C::col_s(slot), m.slab_mask(G));
+        m.pv_at(vslot, C::col_s(slot), m.slab_mask(G));
         if (j + 2 < n_kt) {
           m.qk(base + ring_k1(j + 2), C::col_s(slot), q1_base);
           m.commit(&bars->s_full[slot]);
@@ -1043,6 +1038,40 @@ __device__ void p_mma(const TcFwdParams& p, uint8_t* smem, PBars* bars, const Wa
     base += C::kLoadsPerTile * n_kt;
   }
   if (!m.ok || !ok) m.drain(&bars->drain);
+}
+
+// QK issuer of the rectified form (warp 10): S_G = Q K_G^T into slot G % 3
+// once PV_{G-3}, which read P from that slot, has run (the slots continue
+// across items); the K entry is acquired before that wait.  The item's last
+// QK releases its query buffer (q_empty).
+template <int D>
+__device__ void p_mma_qk(const TcFwdParams& p, uint8_t* smem, PBars* bars, const WaitCtl& ctl, uint32_t tmem) {
+  using C = PCfg<D, false>;
+  MmaIssuer<D, false, C, PBars> m(smem, bars, ctl, tmem);
+  int g = 0, base = 0;
+  bool ok = true;
+  for (int it = 0;; ++it) {
+    const int idx = take_item(bars, it, ctl, ST_MMA_ITEM, ok, false, 0);
+    if (idx < 0 || !ok || !m.ok) break;
+    int bh, qt;
+    decode_item(p, idx, bh, qt);
+    const int n_kt = p.causal_skip ? qt + 1 : p.n_qtiles;
+    const int b = it & 1;
+    m.wait(&bars->q_full[b], (it >> 1) & 1, ST_MMA_Q);
+    const uint32_t q1_base = smem_u32(smem + b * C::kQBytes);
+    for (int t = 0; t < n_kt && m.ok; ++t) {
+      const int G = g + t, slot = G % C::kSSlots;
+      // ring order per item: K_0, K_1, K_2, then per j: V_j, K_{j+3}
+      const int kslot = m.acquire(base + (t < C::kSSlots ? t : ring_v_rect(t - C::kSSlots, n_kt) + 1));
+      if (G >= C::kSSlots) m.wait(&bars->pv_done[slot], ((G - C::kSSlots) / C::kSSlots) & 1, ST_MMA_P);
+      m.qk_at(kslot, C::col_s(slot), q1_base);
+      m.commit(&bars->s_full[slot]);
+      if (t == n_kt - 1) m.commit(&bars->q_empty[b]);
+    }
+    g += n_kt;
+    base += C::kLoadsPerTile * n_kt;
+  }
+  if (!m.ok || !ok) m.drain(&bars->drain2);
 }
 
 template <int D>
@@ -1326,7 +1355,7 @@ __global__ void __maxnreg__(168) tda_tc_fwd_persistent_kernel(const __grid_const
       mbar_init(&bars->q_full[i], 1);
       mbar_init(&bars->q_empty[i], DIFF ? 3 : 2);
       mbar_init(&bars->item_full[i], 1);
-      mbar_init(&bars->item_empty[i], 1 + (DIFF ? 1 : 0) + kTransformWarps);
+      mbar_init(&bars->item_empty[i], 2 + kTransformWarps);
       mbar_init(&bars->s2_free[i], kTransformWarps);
       bars->item[i] = -1;
     }
@@ -1337,6 +1366,7 @@ __global__ void __maxnreg__(168) tda_tc_fwd_persistent_kernel(const __grid_const
     for (int i = 0; i < 3; ++i) {
       mbar_init(&bars->s_full[i], DIFF ? 2 : 1);
       mbar_init(&bars->p_full[i], kTransformWarps);
+      mbar_init(&bars->pv_done[i], 1);
       bars->tile_mask[i] = 0;
     }
     for (int i = 0; i < kRkRing; ++i) {
@@ -1374,8 +1404,13 @@ __global__ void __maxnreg__(168) tda_tc_fwd_persistent_kernel(const __grid_const
     __syncwarp();
   } else if (warp < kQk2Warp) {
     p_transform<D, DIFF, NORM, POS, PM>(p, smem, bars, ctl, tmem, warp, lane);
-  } else if constexpr (DIFF) {
-    if (lane == 0) p_mma_qk2<D>(p, smem, bars, ctl, tmem);
+  } else {
+    if (lane == 0) {
+      if constexpr (DIFF)
+        p_mma_qk2<D>(p, smem, bars, ctl, tmem);
+      else
+        p_mma_qk<D>(p, smem, bars, ctl, tmem);
+    }
     __syncwarp();
   }
   tc_fence_before();
@@ -1478,10 +1513,10 @@ cudaError_t dispatch_diff(const TcFwdParams& p, bool diff, bool norm, int pm, bo
 // word with a running one, which would then skip work items.
 __device__ unsigned g_item_ctr[1024];
 
-// Kernel choice.  The one-CTA-per-tile kernel is the default: with its PV and
-// QK products issued from separate threads it measured 0.501 ms at rect bf16
-// (4,32,4096,128) against 0.524 ms for the persistent kernel, equal at
-// (4,32,2048,128), and ahead at S = 8192 and for the differential form.
+// Kernel choice.  The one-CTA-per-tile kernel is the default: it measured
+// 0.531 ms at rect bf16 (4,32,4096,128) against 0.528 ms for the persistent
+// kernel (both with split PV / QK issuers), and ahead everywhere else
+// (rect (4,32,2048,128) +2%, S = 8192 +3% rect / +13% differential).
 // TDA_B200_FWD_PERSISTENT=1 selects the persistent kernel (=0 or unset: not).
 static bool use_persistent_forward(bool /*differential*/, int /*head_dim*/, int /*n_qtiles*/) {
   static const bool forced = [] {
