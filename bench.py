@@ -579,6 +579,22 @@ def run_tda(args, rank, local, world):
     barrier()
     clk = clocks.stop() if clocks else None
     ops.check_status(dev)
+    # executed tensor-core work of the main kernel, counted in one more
+    # (untimed) launch: the 16-key P.V slabs it multiplied against those a
+    # dense P.V would multiply (bf16 / fp16 tensor-core path)
+    pv_slabs = None
+    if not f32:
+        cnt = torch.zeros(2, dtype=torch.int64, device=dev)
+        _lib.check(lib.tda_debug_stats(cnt.data_ptr()))
+        try:
+            launch_norms()
+            launch_main()
+            torch.cuda.synchronize(dev)
+        finally:
+            _lib.check(lib.tda_debug_stats(None))
+        issued, dense = (int(x) for x in cnt.tolist())
+        if dense > 0:
+            pv_slabs = (issued, dense)
     total_ms = ev[0][0].elapsed_time(ev[-1][2])
     main_ms = [ev[i][1].elapsed_time(ev[i][2]) for i in range(args.steps)]
     norm_ms = [ev[i][0].elapsed_time(ev[i][1]) for i in range(args.steps)]
@@ -600,6 +616,21 @@ def run_tda(args, rank, local, world):
         peak = 148 * 128 * 2 * 1.965e9 / 1e12
         peak_note = "nominal FFMA peak, 148 SMs x 128 lanes x 2 x 1.965 GHz"
     achieved = flops_of(op, n_bh, S, D) / (main_avg / 1e3) / 1e12  # this rank's launch
+    executed = None
+    if pv_slabs:
+        # tensor-core work the main kernel ran on this rank: every QK product of
+        # the (query tile, key tile) pairs it processed (dense / 8 of them, 8
+        # 16-key slabs per tile) and the hi + lo products of each P.V slab it
+        # multiplied (P is split into two bf16 / fp16 parts)
+        issued, dense = pv_slabs
+        n_qk = 2 if op == "diff" else 1
+        kt = 128  # query / key tile edge of the tensor-core kernels
+        ex = dense // 8 * n_qk * 2 * kt * kt * D + issued * 2 * 2 * kt * 16 * D
+        executed = {"pv_slabs_issued": issued, "pv_slabs_dense": dense, "pv_issued_frac": issued / dense,
+                    "tflops": ex / (main_avg / 1e3) / 1e12, "frac_of_peak": ex / (main_avg / 1e3) / 1e12 / peak,
+                    "how": "one extra untimed launch with tda_debug_stats counters; all QK products of the "
+                           "processed tiles plus hi + lo products of the multiplied P.V slabs, over the "
+                           "timed mean main-kernel time"}
 
     # ---- end to end through the public API with pinned host buffers
     # host copies keep the device layout (the storage of a bshd view)
@@ -722,6 +753,7 @@ def run_tda(args, rank, local, world):
                 "traffic": traffic,
                 "peak_source": peak_note,
             },
+            "executed": executed,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": "TFLOP/s",
                     "how": f"public API on {n_chunks} chunks of (batch, head) slices per rank; pinned-host "

@@ -236,6 +236,13 @@ int tda_diff_fwd_noalloc(const void* q1, const void* q2, const void* k1, const v
  * wait_timeout_ns of 0 keeps the default (1 s).  Process-wide setting. */
 int tda_debug_set(int inject, uint64_t wait_timeout_ns);
 
+/* Diagnostic (no counterpart in the reference): with `counters` pointing at
+ * two zeroed uint64 on the device, every later bf16 / fp16 tensor-core forward
+ * launch adds [0] the number of 16-key P.V slabs it multiplied and [1] the
+ * number a dense P.V would have multiplied (causally skipped key tiles count
+ * in neither).  NULL turns it off (the default).  Process-wide setting. */
+int tda_debug_stats(void* counters);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,7 @@ SIGNATURES = {
     "tda_rect_fwd_tc": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _I64, _F, _F, _I, _P, _P, _P]),
     "tda_diff_fwd_tc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _F, _F, _F, _I, _P, _P, _P, _P]),
     "tda_debug_set": (_I, [_I, ctypes.c_uint64]),
+    "tda_debug_stats": (_I, [_P]),
     "tda_diff_fwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I64, _I64, _I64, _F, _F, _F, _I, _P, _P]),
     "tda_rect_fwd_strided": (_I, [_P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _F, _F, _I, _P, _SZ, _P, _P]),
     "tda_diff_fwd_strided": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _F, _F, _F, _I, _P, _SZ,

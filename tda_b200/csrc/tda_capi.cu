@@ -19,6 +19,7 @@ namespace {
 thread_local std::string g_last_error;
 std::atomic<int> g_inject{0};
 std::atomic<unsigned long long> g_timeout_ns{1000000000ull};
+std::atomic<unsigned long long*> g_stats{nullptr};
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -231,6 +232,7 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
   prm.o_unscale = 1.0f / p_scale;
   prm.timeout_ns = g_timeout_ns.load();
   prm.inject = g_inject.load();
+  prm.stats = g_stats.load();
   cudaError_t ce = tda::launch_tc_fwd(prm, static_cast<int>(D), differential, normalize != 0, tda::pow_mode_of(p),
                                       f16, static_cast<cudaStream_t>(stream));
   if (ce == cudaErrorLaunchOutOfResources && !g_last_error.empty() &&
@@ -342,6 +344,11 @@ extern "C" {
 int tda_version(void) { return 101; }
 
 const char* tda_last_error(void) { return g_last_error.c_str(); }
+
+int tda_debug_stats(void* counters) {
+  g_stats.store(static_cast<unsigned long long*>(counters));
+  return TDA_OK;
+}
 
 int tda_debug_set(int inject, uint64_t wait_timeout_ns) {
   g_inject.store(inject);

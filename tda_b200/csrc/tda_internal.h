@@ -81,6 +81,9 @@ struct TcFwdParams {
   unsigned long long timeout_ns;
   int inject;         // test hook: bit 0 = producer never loads Q (forces a timeout)
   unsigned* item_ctr;  // persistent kernel: zeroed work-item counter (null: one CTA per query tile)
+  // diagnostics (null: off): [0] += 16-key PV slabs multiplied, [1] += slabs a
+  // dense PV would multiply, per query tile (one atomic add each per CTA)
+  unsigned long long* stats;
 };
 
 // fp16 = true: q, k, v (and the output, unless fp32) are fp16 -- kind::f16 with

@@ -290,6 +290,7 @@ struct MmaIssuer {
   uint32_t ring_base;
   bool ok;
   bool o_started;
+  unsigned slabs = 0;  // 16-key slabs multiplied by pv (diagnostics)
 
   __device__ MmaIssuer(uint8_t* smem, B* b, const WaitCtl& c, uint32_t t)
       : bars(b), ctl(c), tmem(t), ring_base(smem_u32(smem + C::kOffRing)), ok(true), o_started(false) {}
@@ -331,6 +332,7 @@ struct MmaIssuer {
       return;
     }
     const uint32_t v_base = ring_base + slot * C::kTileBytes;
+    slabs += __popc(mask);
 #pragma unroll
     for (int m = 0; m < kTile / 16; ++m) {
       if (!(mask & (1u << m))) continue;
@@ -379,7 +381,8 @@ __device__ __forceinline__ int ring_v_rect(int j, int n_kt) {
 //     32 KB ring slots for three tiles per key step the K1 load is often
 //     still in flight, and waiting for it first would hold PV_j back.
 template <int D, bool DIFF, bool F16>
-__device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
+__device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt,
+                        unsigned long long* stats) {
   using C = Cfg<D, DIFF>;
   MmaIssuer<D, DIFF, C, Bars, F16> m(smem, bars, ctl, tmem);
   const uint32_t q1_base = smem_u32(smem);
@@ -408,6 +411,10 @@ __device__ void run_mma(uint8_t* smem, Bars* bars, const WaitCtl& ctl, uint32_t 
     tc_commit(&bars->o_full);
   else
     m.drain(&bars->drain);
+  if (stats) {
+    atomicAdd(stats, static_cast<unsigned long long>(m.slabs));
+    atomicAdd(stats + 1, static_cast<unsigned long long>(n_kt) * (kTile / 16));
+  }
 }
 
 // QK issuer of the rectified form (warp 10).  The first three products go
@@ -707,7 +714,7 @@ __global__ void __maxnreg__((Cfg<D, DIFF>::kMaxRegs)) tda_tc_fwd_kernel(const __
     if (lane == 0) run_producer<D, DIFF, NORM>(p, smem, bars, ctl, bh, qt, n_kt);
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) run_mma<D, DIFF, F16>(smem, bars, ctl, tmem, n_kt);
+    if (lane == 0) run_mma<D, DIFF, F16>(smem, bars, ctl, tmem, n_kt, p.stats);
     __syncwarp();
   } else if (warp < C::kQk2W) {
     run_transform<D, DIFF, NORM, POS, PM, F16>(p, smem, bars, ctl, tmem, bh, qt, n_kt, warp, lane);
@@ -1038,6 +1045,10 @@ __device__ void p_mma(const TcFwdParams& p, uint8_t* smem, PBars* bars, const Wa
     base += C::kLoadsPerTile * n_kt;
   }
   if (!m.ok || !ok) m.drain(&bars->drain);
+  if (p.stats) {
+    atomicAdd(p.stats, static_cast<unsigned long long>(m.slabs));
+    atomicAdd(p.stats + 1, static_cast<unsigned long long>(g) * (kTile / 16));
+  }
 }
 
 // QK issuer of the rectified form (warp 10): S_G = Q K_G^T into slot G % 3

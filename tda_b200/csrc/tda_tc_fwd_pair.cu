@@ -296,6 +296,7 @@ struct PairIssuer {
   uint32_t ring_base;
   bool ok;
   bool o_started;
+  unsigned slabs = 0;  // 16-key slabs multiplied by pv_at, per CTA of the pair (diagnostics)
 
   __device__ PairIssuer(uint8_t* smem, PairBars* b, const WaitCtl& c, uint32_t t)
       : bars(b), ctl(c), tmem(t), ring_base(smem_u32(smem + C::kOffRing)), ok(true), o_started(false) {}
@@ -352,6 +353,7 @@ struct PairIssuer {
       return;
     }
     const uint32_t v_base = ring_base + slot * C::kHalfBytes;
+    slabs += __popc(mask);
 #pragma unroll
     for (int m = 0; m < kTile / 16; ++m) {
       if (!(mask & (1u << m))) continue;
@@ -388,7 +390,8 @@ struct PairIssuer {
 // (Issuing QK1 from the QK2 thread instead, after PV_j has completed, measured
 // 12% slower: the wait for PV_j's completion delays S1 of tile j + 2.)
 template <bool DIFF, bool F16>
-__device__ void run_pair_mma(uint8_t* smem, PairBars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt) {
+__device__ void run_pair_mma(uint8_t* smem, PairBars* bars, const WaitCtl& ctl, uint32_t tmem, int n_kt,
+                             unsigned long long* stats) {
   using C = PairCfg<DIFF>;
   PairIssuer<DIFF, F16> m(smem, bars, ctl, tmem);
   const uint32_t q1_base = smem_u32(smem);
@@ -418,6 +421,10 @@ __device__ void run_pair_mma(uint8_t* smem, PairBars* bars, const WaitCtl& ctl, 
     m.commit_both(&bars->o_full);
   else
     m.drain(&bars->drain);
+  if (stats) {  // a slab of the pair serves both CTAs' query tiles
+    atomicAdd(stats, 2ull * m.slabs);
+    atomicAdd(stats + 1, 2ull * n_kt * (kTile / 16));
+  }
 }
 
 // Leader warp 10, rect: QK_{j+3} into P_j's slot once PV_j has run.
@@ -706,7 +713,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(168)
   } else if (warp == 1) {
     if (lane == 0) {
       if (rank == 0) {
-        run_pair_mma<DIFF, F16>(smem, bars, ctl, tmem, n_kt);
+        run_pair_mma<DIFF, F16>(smem, bars, ctl, tmem, n_kt, p.stats);
       } else if (!(p.inject & 1)) {
         // the leader's products read this CTA's query tile(s) too
         if (mbar_wait(&bars->q_full, 0, ctl, ST_PM_Q)) mbar_arrive_cluster(leader_addr(&bars->q_pair));
