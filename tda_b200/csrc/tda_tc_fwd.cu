@@ -77,12 +77,15 @@ constexpr int ST_TR_Q = 0x301, ST_TR_RK = 0x302, ST_TR_S = 0x303, ST_TR_O = 0x30
 // single-thread issuers so that one issuer's waits and commits (each some
 // 100-200 cycles of latency on a single thread) overlap the other's MMAs:
 // warp 1 issues every PV (and QK1 for the differential form), warp 10 the QK
-// products (rect) or QK2 (differential).  (Four warpgroups with one chunk per thread --
-// kTWG = 4, which this code also supports -- measured 4-8% slower on B200:
-// the transform's per-warp instruction latency is not what bounds a tile.)
+// products (rect) or QK2 (differential).  Two transform warpgroups, two
+// 32-key chunks per thread.  Four (one chunk per thread, 608 threads, 96
+// registers; kTWG = 4 is supported and bit-identical) measured, A/B on one
+// box: rect +3.5% at (4,32,2048,128), +1.8% at (4,32,4096,128), equal at
+// (8,32,8192,128), but -3.6% with dense P (beta = 0) there; differential -8%.
 template <int D, bool DIFF>
 struct Cfg {
   static constexpr int kTWG = 2;                 // transform warpgroups
+  static constexpr int kSumWG = 2;               // warpgroups summing the query norms
   static constexpr int kTW = 4 * kTWG;           // transform warps 2 .. 1 + kTW
   static constexpr int kQk2W = 2 + kTW;          // QK issuer (rect) / QK2 issuer (differential)
   static constexpr int kThreads = 32 * (3 + kTW);
@@ -94,7 +97,7 @@ struct Cfg {
   static constexpr int kRkPerTile = (DIFF ? 2 : 1) * (kTile + 8);  // rk then per-16-key maxima
   static constexpr int kRkFloats = kRkRing * kRkPerTile;
   static constexpr int kBarBytes = 1024;
-  static constexpr int kQssBytes = kNQ * kTWG * kTile * 4;  // partial sums of ||q||^2
+  static constexpr int kQssBytes = kNQ * kSumWG * kTile * 4;  // partial sums of ||q||^2
   static constexpr int kFixed = kNQ * kTileBytes + kRkFloats * 4 + kBarBytes + kQssBytes + 1024;
   static constexpr int kSlotsRaw = (kSmemBudget - kFixed) / kTileBytes;
   static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
@@ -471,7 +474,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
   using C = Cfg<D, DIFF>;
   constexpr bool kFold = PM != POW_GENERAL;
   constexpr int kChunks = 4 / C::kTWG;  // 32-key chunks per thread per tile
-  constexpr int kQChunks = 8 / C::kTWG;  // 16-B chunks of each 128-B query row this warpgroup sums
+  constexpr int kQChunks = 8 / C::kSumWG;  // 16-B chunks of each 128-B query row a summing warpgroup sums
   const int wg = (warp - 2) >> 2;
   const int quarter = warp & 3;
   const int row = quarter * 32 + lane;
@@ -493,12 +496,14 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
   if constexpr (NORM) {
     ok = mbar_wait_warp(&bars->q_full, 0, ctl, ST_TR_Q);
     // ||q_i|| from the swizzled tile(s): row r's 16-B chunks are permuted
-    // within the row only, so summing chunks needs no unswizzle.  The two
-    // warpgroups (which own the same rows) each sum half of every row's
-    // chunks and exchange the partial sums through shared memory.  A rolled
-    // loop keeps this once-per-CTA code small in the instruction cache.
-    float* qss = reinterpret_cast<float*>(smem + C::kOffQss);  // [kNQ][kTWG][kTile]
-    if (ok) {
+    // within the row only, so summing chunks needs no unswizzle.  Warpgroups
+    // 0 and 1 (which own the same rows) each sum half of every row's chunks
+    // and exchange the partial sums through shared memory -- with four
+    // warpgroups too, so that the norms (and every result) are bit-identical
+    // to the two-warpgroup kernels.  A rolled loop keeps this once-per-CTA
+    // code small in the instruction cache.
+    float* qss = reinterpret_cast<float*>(smem + C::kOffQss);  // [kNQ][kSumWG][kTile]
+    if (ok && wg < C::kSumWG) {
 #pragma unroll 1
       for (int t = 0; t < C::kNQ; ++t) {
         float ss = 0.0f;
@@ -520,7 +525,7 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
             }
           }
         }
-        qss[(t * C::kTWG + wg) * kTile + row] = ss;
+        qss[(t * C::kSumWG + wg) * kTile + row] = ss;
       }
     }
     // every transform thread arrives, also one whose wait gave up
@@ -528,9 +533,9 @@ __device__ void run_transform(const TcFwdParams& p, uint8_t* smem, Bars* bars, c
     if (ok) {
       float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
-      for (int g = 0; g < C::kTWG; ++g) {
+      for (int g = 0; g < C::kSumWG; ++g) {
         s1 += qss[g * kTile + row];
-        if constexpr (DIFF) s2 += qss[(C::kTWG + g) * kTile + row];
+        if constexpr (DIFF) s2 += qss[(C::kSumWG + g) * kTile + row];
       }
       const float m1 = fmaxf(sqrtf(s1), 1e-12f);
       c.rq1 = 1.0f / m1;
