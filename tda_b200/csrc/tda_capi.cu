@@ -206,7 +206,7 @@ int run_tc(const View& q1, const View& q2, const View& k1, const View& k2, const
     if ((e = make_map4(&prm.tm_q2, q2, batches, heads, S, D, f16))) return e;
     if ((e = make_map4(&prm.tm_k2, k2, batches, heads, S, D, f16))) return e;
   }
-  if (D == 128) {  // the CTA-pair kernel loads half key tiles (64 rows)
+  if (tda::tc_fwd_uses_pair(static_cast<int>(D))) {  // the CTA-pair kernel loads half key tiles (64 rows)
     if ((e = make_map4(&prm.tm_k1h, k1, batches, heads, S, D, f16, tda::kTile / 2))) return e;
     if (differential && (e = make_map4(&prm.tm_k2h, k2, batches, heads, S, D, f16, tda::kTile / 2))) return e;
   }

@@ -90,6 +90,9 @@ struct TcFwdParams {
 // fp16 operands, P split into fp16 hi + lo; only with normalize (P bounded).
 cudaError_t launch_tc_fwd(const TcFwdParams& p, int head_dim, bool differential, bool normalize, int pow_mode,
                           bool fp16, cudaStream_t stream);
+// Whether launch_tc_fwd runs the CTA-pair kernel at this head dim (then the
+// caller sets tm_k1h / tm_k2h).
+bool tc_fwd_uses_pair(int head_dim);
 // The same forward at head_dim 128 on CTA pairs (tm_k1h / tm_k2h set).
 cudaError_t launch_tc_fwd_pair(const TcFwdParams& p, bool differential, bool normalize, int pow_mode, bool fp16,
                                cudaStream_t stream);

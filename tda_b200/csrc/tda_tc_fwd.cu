@@ -1580,12 +1580,15 @@ static bool use_pair_forward(int head_dim) {
   return on && head_dim == 128;
 }
 
+bool tc_fwd_uses_pair(int head_dim) {
+  return use_pair_forward(head_dim) && !use_persistent_forward(false, head_dim, 0);
+}
+
 cudaError_t launch_tc_fwd(const TcFwdParams& p_in, int head_dim, bool differential, bool normalize, int pow_mode,
                           bool fp16, cudaStream_t stream) {
   TcFwdParams p = p_in;
   p.item_ctr = nullptr;
-  if (use_pair_forward(head_dim) && !use_persistent_forward(differential, head_dim, p.n_qtiles))
-    return launch_tc_fwd_pair(p, differential, normalize, pow_mode, fp16, stream);
+  if (tc_fwd_uses_pair(head_dim)) return launch_tc_fwd_pair(p, differential, normalize, pow_mode, fp16, stream);
   if (!fp16 && use_persistent_forward(differential, head_dim, p.n_qtiles)) {
     cudaError_t e = prepare_item_counter(p, stream);
     if (e != cudaSuccess) return e;
