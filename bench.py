@@ -45,6 +45,9 @@ WORKLOADS = {
     "diff32k": ("diff", 1, 16, 32768, 128, 1.5, 0.8, 2.0, True),
     # one rank's share of BASELINE config 4 on 8 GPUs (2 of its 16 heads), timed on one GPU
     "diff32k_share8": ("diff", 1, 2, 32768, 128, 1.5, 0.8, 2.0, True),
+    # one rank's share of the headline on 8 GPUs (32 of its 256 (batch, head) slices)
+    "diff8k_share8": ("diff", 1, 32, 8192, 128, 1.0, 0.5, 2.0, True),
+    "rect8k_share8": ("rect", 1, 32, 8192, 128, 1.0, 0.0, 2.0, True),
     # beta = 0 with normalize: P is nonzero wherever cos > 0 (about half the
     # entries), the dense worst case for the transform
     "diff8k_dense": ("diff", 8, 32, 8192, 128, 0.0, 0.5, 2.0, True),
